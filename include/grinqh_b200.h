@@ -1,0 +1,133 @@
+/*
+ * grinqh_b200.h -- C ABI of the B200 (sm_100a) GRINQH quantized-linear hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream; no torch types. Every pointer named
+ * `*_dev` is device memory; thresholds are host memory. All entry points are
+ * asynchronous on `stream` (no host synchronisation, no device->host reads), so
+ * they can be recorded into CUDA graphs, and return a grinqh_status code
+ * (GRINQH_OK == 0). On error, grinqh_last_error() returns a message for the
+ * calling thread.
+ *
+ * Reference interfaces replaced (paths relative to the reference project root):
+ *   grinqh_pack_words        <- grinqh/utils.py:125-146  pack_triton / _pack_kernel_uint32 (:100-122)
+ *   grinqh_pack_codes        <- grinqh/grinqh.py:202-211 process_weights_after_loading
+ *                               (grinqh_input_preshuffle utils.py:17-22, << (8-b), pack_triton)
+ *   grinqh_unpack            <- grinqh/utils.py:149-177  unpack_pyt, :209-223 unpack_triton
+ *   grinqh_grade             <- grinqh/kernel.py:100-116 threshold masks of the graded GEMV
+ *   grinqh_gemm_or_gemv      <- grinqh/kernel.py:646-710 torch.ops.grinqh.gemm_or_gemv
+ *   grinqh_gemv_batch_union  <- grinqh/kernel.py:607-643 grinqh_gemv_batch_union
+ *   grinqh_prefill_gemm      <- grinqh/kernel.py:561-587 grinqh_prefill_gemm_compiled
+ *
+ * Tensor layouts (row-major, contiguous unless a leading dimension is given):
+ *   x              [M, K]            activations, dtype (bf16 or fp16)
+ *   weight_packed  [K, (b/2)*N/16]   uint32 bit planes (grinqh/utils.py:100-122 layout)
+ *   weight_scale   [K/group, N]      dtype, one scale per (K group, output column)
+ *   bias           [N] or NULL       dtype
+ *   y              [M, N]            dtype
+ * with b = max_bits in {2,4,6,8}, N % 16 == 0, K % group_size == 0,
+ * group_size % 32 == 0, and N == 4 * original_n of the reference signature.
+ */
+#ifndef GRINQH_B200_H
+#define GRINQH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Identical to cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *grinqh_stream_t;
+
+typedef enum grinqh_status {
+  GRINQH_OK = 0,
+  GRINQH_ERR_INVALID = 1,     /* bad argument: null pointer, shape, alignment       */
+  GRINQH_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. max_bits = 3)       */
+  GRINQH_ERR_CUDA = 3,        /* CUDA launch / runtime error                         */
+  GRINQH_ERR_WORKSPACE = 4,   /* workspace missing or smaller than required          */
+  GRINQH_ERR_DEVICE = 5       /* current device is not an sm_100 (B200-class) GPU    */
+} grinqh_status;
+
+typedef enum grinqh_dtype {
+  GRINQH_F16 = 0,
+  GRINQH_BF16 = 1
+} grinqh_dtype;
+
+/* How rows of x pick the weight planes they read (grinqh_gemm_or_gemv):
+ *   AUTO   -- the reference dispatch (kernel.py:663-705): one row -> graded GEMV,
+ *             several rows -> dense x @ dtype(w*s), thresholds ignored;
+ *   DENSE  -- always the dense path;
+ *   GRADED -- every row graded by its own activations (the reference's one-row
+ *             GEMV applied row by row; this build's opt-in graded prefill);
+ *   UNION  -- rows graded by max_m |x[m,k]| (grinqh_gemv_batch_union semantics). */
+typedef enum grinqh_mode {
+  GRINQH_MODE_AUTO = 0,
+  GRINQH_MODE_DENSE = 1,
+  GRINQH_MODE_GRADED = 2,
+  GRINQH_MODE_UNION = 3
+} grinqh_mode;
+
+int grinqh_abi_version(void);
+const char *grinqh_status_string(int status);
+const char *grinqh_last_error(void);
+
+/* Bit-plane pack of already preshuffled and shifted code words.
+ * words_dev [K, n_words] uint32 (4 code bytes per word, codes in the MSBs),
+ * n_words % 4 == 0; out_dev [K, (b/2)*n_words/4] uint32.
+ * Replaces pack_triton (grinqh/utils.py:125-146), bit-exact. */
+int grinqh_pack_words(const uint32_t *words_dev, uint32_t *out_dev, int64_t K, int64_t n_words,
+                      int max_bits, grinqh_stream_t stream);
+
+/* Load-time transform fused in one pass: column preshuffle, << (8-b), pack.
+ * codes_dev [K, N] int8 signed codes in [-2^(b-1), 2^(b-1)-1] (K-major, row stride ld >= N);
+ * out_dev [K, (b/2)*N/16] uint32. Replaces grinqh/grinqh.py:202-211, bit-exact. */
+int grinqh_pack_codes(const int8_t *codes_dev, int64_t ld, uint32_t *out_dev, int64_t K, int64_t N,
+                      int max_bits, grinqh_stream_t stream);
+
+/* Inverse of grinqh_pack_words: out_dev [K, N] uint8, byte = shifted_code >> (8-b)
+ * (unsigned, preshuffled column order), exactly unpack_pyt (grinqh/utils.py:149-177). */
+int grinqh_unpack(const uint32_t *packed_dev, uint8_t *out_dev, int64_t K, int64_t N, int max_bits,
+                  grinqh_stream_t stream);
+
+/* Grade activations: masks_dev [M, K] uint8 with bit z set iff fp32|x[m,k]| > fp32(t_z)
+ * for z < b/2 (strict; NaN never active), grinqh/kernel.py:100-116.
+ * union_dev [K] uint8 (may be NULL) = OR over rows. thresholds: 4 host floats. */
+int grinqh_grade(const void *x_dev, int dtype, int64_t M, int64_t K, const float *thresholds,
+                 int max_bits, uint8_t *masks_dev, uint8_t *union_dev, grinqh_stream_t stream);
+
+/* Scratch bytes grinqh_gemm_or_gemv / grinqh_gemv_batch_union / grinqh_prefill_gemm
+ * need for these sizes and mode (0 is possible). */
+size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int mode);
+
+/* The quantized linear y = x @ W (+ bias), torch.ops.grinqh.gemm_or_gemv
+ * (grinqh/kernel.py:646-710). workspace_dev: grinqh_workspace_size() bytes,
+ * 256-byte aligned; its contents need no initialisation and are not preserved.
+ * thresholds: 4 host floats (ignored by DENSE / AUTO with M > 1). */
+int grinqh_gemm_or_gemv(const void *x_dev, int dtype, int64_t M, int64_t K,
+                        const uint32_t *weight_packed_dev, const void *weight_scale_dev,
+                        const void *bias_dev, int max_bits, int group_size, int64_t N,
+                        const float *thresholds, int mode, void *y_dev, void *workspace_dev,
+                        size_t workspace_bytes, grinqh_stream_t stream);
+
+/* Small-batch GEMV graded by the row union (grinqh/kernel.py:607-643); same as
+ * grinqh_gemm_or_gemv with mode = GRINQH_MODE_UNION. */
+int grinqh_gemv_batch_union(const void *x_dev, int dtype, int64_t M, int64_t K,
+                            const uint32_t *weight_packed_dev, const void *weight_scale_dev,
+                            const void *bias_dev, int max_bits, int group_size, int64_t N,
+                            const float *thresholds, void *y_dev, void *workspace_dev,
+                            size_t workspace_bytes, grinqh_stream_t stream);
+
+/* Dense path y = x @ dtype(w * s) for any M >= 1 (grinqh/kernel.py:561-587); same as
+ * grinqh_gemm_or_gemv with mode = GRINQH_MODE_DENSE. */
+int grinqh_prefill_gemm(const void *x_dev, int dtype, int64_t M, int64_t K,
+                        const uint32_t *weight_packed_dev, const void *weight_scale_dev,
+                        const void *bias_dev, int max_bits, int group_size, int64_t N,
+                        void *y_dev, void *workspace_dev, size_t workspace_bytes,
+                        grinqh_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRINQH_B200_H */

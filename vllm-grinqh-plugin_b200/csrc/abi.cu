@@ -1,0 +1,178 @@
+// C ABI entry points of the quantized linear and shared status plumbing.
+#include <mutex>
+
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace grinqh {
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int kMaxDevices = 64;
+int g_cc_major[kMaxDevices];  // 0 = unknown
+int g_sm_count[kMaxDevices];
+std::mutex g_dev_mu;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+int set_error(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return GRINQH_OK;
+}
+
+static int device_info(int* dev_out, int* sm_count) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(GRINQH_ERR_DEVICE, "device ordinal %d out of range", dev);
+  if (g_cc_major[dev] == 0) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    int major = 0, sms = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    g_sm_count[dev] = sms;
+    g_cc_major[dev] = major;
+  }
+  if (g_cc_major[dev] != 10)
+    return set_error(GRINQH_ERR_DEVICE, "device %d has compute capability %d.x; this library is built for sm_100a",
+                     dev, g_cc_major[dev]);
+  if (dev_out) *dev_out = dev;
+  if (sm_count) *sm_count = g_sm_count[dev];
+  return GRINQH_OK;
+}
+
+int check_device() { return device_info(nullptr, nullptr); }
+
+struct LinearShape {
+  int64_t M, K, N;
+  int bits, group, mode;
+};
+
+// Map the public mode to a kernel mode (grinqh/kernel.py:663-705 dispatch for AUTO).
+static int resolve_mode(int mode, int64_t M) {
+  switch (mode) {
+    case GRINQH_MODE_AUTO: return M == 1 ? kModeGraded : kModeDense;
+    case GRINQH_MODE_DENSE: return kModeDense;
+    case GRINQH_MODE_GRADED: return kModeGraded;
+    case GRINQH_MODE_UNION: return kModeUnion;
+    default: return -1;
+  }
+}
+
+static size_t workspace_for(const DecodePlan& p) {
+  if (p.ksplit <= 1) return 0;
+  return align_up(p.partial_bytes, 256) + align_up(p.counter_bytes, 256);
+}
+
+static int validate(const void* x, int dtype, int64_t M, int64_t K, const void* w, const void* s, int bits,
+                    int group, int64_t N, const void* y) {
+  if (!valid_bits(bits)) return set_error(GRINQH_ERR_UNSUPPORTED, "max_bits must be 2, 4, 6 or 8 (got %d)", bits);
+  GRINQH_REQUIRE(dtype == GRINQH_BF16 || dtype == GRINQH_F16, "dtype must be GRINQH_BF16 or GRINQH_F16");
+  GRINQH_REQUIRE(M >= 0, "M must be >= 0");
+  GRINQH_REQUIRE(K > 0, "K must be > 0");
+  GRINQH_REQUIRE(N > 0 && N % 16 == 0, "N must be a positive multiple of 16 (got %lld)", (long long)N);
+  GRINQH_REQUIRE(group > 0 && group % 32 == 0, "group_size must be a positive multiple of 32 (got %d)", group);
+  GRINQH_REQUIRE(K % group == 0, "K (%lld) must be a multiple of group_size (%d)", (long long)K, group);
+  GRINQH_REQUIRE(K < (1LL << 31) && N < (1LL << 31) && M < (1LL << 31), "size exceeds int32 range");
+  GRINQH_REQUIRE(M == 0 || (x && w && s && y), "null pointer");
+  return GRINQH_OK;
+}
+
+}  // namespace grinqh
+
+using namespace grinqh;
+
+extern "C" int grinqh_abi_version(void) { return 1; }
+
+extern "C" const char* grinqh_status_string(int status) {
+  switch (status) {
+    case GRINQH_OK: return "ok";
+    case GRINQH_ERR_INVALID: return "invalid argument";
+    case GRINQH_ERR_UNSUPPORTED: return "unsupported";
+    case GRINQH_ERR_CUDA: return "CUDA error";
+    case GRINQH_ERR_WORKSPACE: return "workspace too small";
+    case GRINQH_ERR_DEVICE: return "unsupported device";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* grinqh_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int mode) {
+  (void)max_bits;
+  const int km = resolve_mode(mode, M);
+  if (km < 0 || M <= 0 || K <= 0 || N <= 0) return 0;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
+  return workspace_for(plan_decode(M, K, N, km, sms));
+}
+
+extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                   const void* s, const void* bias, int max_bits, int group, int64_t N,
+                                   const float* thresholds, int mode, void* y, void* workspace,
+                                   size_t workspace_bytes, grinqh_stream_t stream) {
+  int dev = 0, sms = 0;
+  GRINQH_RETURN_IF(device_info(&dev, &sms));
+  GRINQH_RETURN_IF(validate(x, dtype, M, K, w, s, max_bits, group, N, y));
+  const int km = resolve_mode(mode, M);
+  GRINQH_REQUIRE(km >= 0, "unknown mode %d", mode);
+  GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
+  if (M == 0) return GRINQH_OK;
+
+  const DecodePlan plan = plan_decode(M, K, N, km, sms);
+  const size_t need = workspace_for(plan);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
+
+  DecodeArgs a{};
+  a.x = x;
+  a.w = w;
+  a.s = s;
+  a.bias = bias;
+  a.y = y;
+  a.M = (int)M;
+  a.K = (int)K;
+  a.N = (int)N;
+  a.group = group;
+  a.rows_per_cta = plan.rows_per_cta;
+  a.ksplit = plan.ksplit;
+  for (int z = 0; z < 4; ++z) a.t[z] = thresholds ? thresholds[z] : 0.0f;
+  if (plan.ksplit > 1) {
+    char* base = static_cast<char*>(workspace);
+    a.partial = reinterpret_cast<float*>(base);
+    a.counters = reinterpret_cast<unsigned*>(base + align_up(plan.partial_bytes, 256));
+    const cudaError_t e = cudaMemsetAsync(a.counters, 0, plan.counter_bytes, stream);
+    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
+  return launch_decode(a, plan, km, dtype, max_bits / 2, stream);
+}
+
+extern "C" int grinqh_gemv_batch_union(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                       const void* s, const void* bias, int max_bits, int group, int64_t N,
+                                       const float* thresholds, void* y, void* workspace, size_t workspace_bytes,
+                                       grinqh_stream_t stream) {
+  return grinqh_gemm_or_gemv(x, dtype, M, K, w, s, bias, max_bits, group, N, thresholds, GRINQH_MODE_UNION, y,
+                             workspace, workspace_bytes, stream);
+}
+
+extern "C" int grinqh_prefill_gemm(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                   const void* s, const void* bias, int max_bits, int group, int64_t N, void* y,
+                                   void* workspace, size_t workspace_bytes, grinqh_stream_t stream) {
+  return grinqh_gemm_or_gemv(x, dtype, M, K, w, s, bias, max_bits, group, N, nullptr, GRINQH_MODE_DENSE, y,
+                             workspace, workspace_bytes, stream);
+}

@@ -1,0 +1,209 @@
+// torch custom ops of the GRINQH plugin. Thin shims: argument checks, output /
+// workspace allocation through the caching allocator, the current CUDA stream,
+// then one call into the C ABI (include/grinqh_b200.h). No CPU implementation is
+// registered: a CPU tensor raises.
+//
+// Schemas mirror the reference's op (grinqh/kernel.py:646-657) plus the helpers
+// its tests call (pack_triton utils.py:125, unpack utils.py:149/209,
+// grinqh_gemv_batch_union kernel.py:607, grinqh_prefill_gemm_compiled kernel.py:561).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <cstdlib>
+#include <optional>
+#include <vector>
+
+#include "grinqh_b200.h"
+
+namespace {
+
+int dtype_code(const at::Tensor& t, const char* name) {
+  if (t.scalar_type() == at::kBFloat16) return GRINQH_BF16;
+  if (t.scalar_type() == at::kHalf) return GRINQH_F16;
+  TORCH_CHECK(false, "GRINQH: ", name, " must be float16 or bfloat16, got ", t.scalar_type());
+  return -1;
+}
+
+void check_ok(int st, const char* what) {
+  TORCH_CHECK(st == GRINQH_OK, "GRINQH ", what, " failed (", grinqh_status_string(st), "): ", grinqh_last_error());
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "GRINQH: ", name, " must be a CUDA tensor (no CPU implementation)");
+}
+
+bool is_word32(const at::Tensor& t) {
+  return t.scalar_type() == at::kInt || t.scalar_type() == at::kUInt32;
+}
+
+std::vector<float> thresholds4(at::ArrayRef<double> th) {
+  // kernel.py:700 reads thresholds[0..3]; grinqh.py:113 pads with 0.0
+  std::vector<float> t(4, 0.0f);
+  for (size_t i = 0; i < th.size() && i < 4; ++i) t[i] = static_cast<float>(th[i]);
+  return t;
+}
+
+cudaStream_t cur_stream(const at::Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+int env_mode_for_rows() {
+  // Opt-in per-token grading for rows > 1 (this build's graded prefill).
+  static const int m = [] {
+    const char* v = std::getenv("GRINQH_GRADED_PREFILL");
+    return (v && v[0] == '1') ? GRINQH_MODE_GRADED : GRINQH_MODE_AUTO;
+  }();
+  return m;
+}
+
+at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                      const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
+                      int64_t original_n, at::ArrayRef<double> thresholds, int mode) {
+  check_cuda(x, "x");
+  check_cuda(weight_packed, "weight_packed");
+  check_cuda(weight_scale, "weight_scale");
+  const int dt = dtype_code(x, "x");
+  TORCH_CHECK(weight_scale.scalar_type() == x.scalar_type(), "GRINQH: weight_scale dtype ", weight_scale.scalar_type(),
+              " != x dtype ", x.scalar_type());
+  TORCH_CHECK(is_word32(weight_packed), "GRINQH: weight_packed must be int32/uint32, got ", weight_packed.scalar_type());
+  TORCH_CHECK(x.dim() >= 1, "GRINQH: x must have at least one dimension");
+  TORCH_CHECK(weight_packed.dim() == 2 && weight_scale.dim() == 2, "GRINQH: weight_packed and weight_scale must be 2-D");
+  const int64_t K = weight_packed.size(0);
+  const int64_t N = original_n * 4;
+  TORCH_CHECK(max_bits == 2 || max_bits == 4 || max_bits == 6 || max_bits == 8,
+              "GRINQH: max_bits must be 2, 4, 6 or 8, got ", max_bits);
+  TORCH_CHECK(x.size(-1) == K, "GRINQH: x.shape[-1] (", x.size(-1), ") != K (", K, ")");
+  TORCH_CHECK(weight_packed.size(1) == (max_bits / 2) * (N / 16), "GRINQH: weight_packed has ", weight_packed.size(1),
+              " columns, expected ", (max_bits / 2) * (N / 16), " for N=", N, " and max_bits=", max_bits);
+  TORCH_CHECK(group_size > 0 && K % group_size == 0, "GRINQH: K must be a multiple of group_size");
+  TORCH_CHECK(weight_scale.size(0) == K / group_size && weight_scale.size(1) == N, "GRINQH: weight_scale shape ",
+              weight_scale.sizes(), " != [", K / group_size, ", ", N, "]");
+  if (bias) {
+    check_cuda(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == x.scalar_type() && bias->numel() == N, "GRINQH: bias must be [N] of x's dtype");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor xf = x.reshape({-1, K}).contiguous();
+  const at::Tensor wp = weight_packed.contiguous();
+  const at::Tensor sc = weight_scale.contiguous();
+  const at::Tensor bc = bias ? bias->contiguous() : at::Tensor();
+  const int64_t M = xf.size(0);
+  std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
+  out_shape.back() = N;
+  at::Tensor y = at::empty({M, N}, x.options());
+  if (M == 0) return y.view(out_shape);
+  const auto th = thresholds4(thresholds);
+  const size_t ws_bytes = grinqh_workspace_size(M, K, N, (int)max_bits, mode);
+  at::Tensor ws;
+  if (ws_bytes) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
+  const int st = grinqh_gemm_or_gemv(xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()),
+                                     sc.data_ptr(), bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N,
+                                     th.data(), mode, y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
+                                     cur_stream(x));
+  check_ok(st, "gemm_or_gemv");
+  return y.view(out_shape);
+}
+
+// torch.ops.grinqh.gemm_or_gemv -- grinqh/kernel.py:646-710. use_marlin is accepted
+// for schema compatibility and ignored (no Marlin path in this build).
+at::Tensor gemm_or_gemv(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                        const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
+                        int64_t original_n, at::ArrayRef<double> thresholds, bool use_marlin) {
+  (void)use_marlin;
+  return run_linear(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds,
+                    env_mode_for_rows());
+}
+
+at::Tensor linear(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                  const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size, int64_t original_n,
+                  at::ArrayRef<double> thresholds, int64_t mode) {
+  TORCH_CHECK(mode >= 0 && mode <= 3, "GRINQH: mode must be 0..3");
+  return run_linear(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds, (int)mode);
+}
+
+// pack_triton (grinqh/utils.py:125-146): [K, N/4] shifted code words -> [K, (b/2)*N/16]
+at::Tensor pack(const at::Tensor& words, int64_t max_bits) {
+  check_cuda(words, "words");
+  TORCH_CHECK(is_word32(words) && words.dim() == 2, "GRINQH pack: expects a 2-D uint32/int32 tensor");
+  const at::Tensor a = words.contiguous();
+  const int64_t K = a.size(0), nw = a.size(1);
+  TORCH_CHECK(nw % 4 == 0, "GRINQH pack: number of words must be a multiple of 4");
+  const c10::cuda::CUDAGuard guard(a.device());
+  at::Tensor out = at::empty({K, (max_bits / 2) * (nw / 4)}, a.options());
+  check_ok(grinqh_pack_words(reinterpret_cast<const uint32_t*>(a.data_ptr()), reinterpret_cast<uint32_t*>(out.data_ptr()),
+                             K, nw, (int)max_bits, cur_stream(a)),
+           "pack");
+  return out;
+}
+
+// process_weights_after_loading transform (grinqh/grinqh.py:202-211) from int8 codes
+at::Tensor pack_codes(const at::Tensor& codes, int64_t max_bits) {
+  check_cuda(codes, "codes");
+  TORCH_CHECK(codes.scalar_type() == at::kChar && codes.dim() == 2, "GRINQH pack_codes: expects 2-D int8 codes [K, N]");
+  const at::Tensor c = codes.stride(1) == 1 ? codes : codes.contiguous();
+  const int64_t K = c.size(0), N = c.size(1);
+  TORCH_CHECK(N % 16 == 0, "GRINQH pack_codes: N must be divisible by 16 for this layout");
+  const c10::cuda::CUDAGuard guard(c.device());
+  at::Tensor out = at::empty({K, (max_bits / 2) * (N / 16)}, c.options().dtype(at::kUInt32));
+  check_ok(grinqh_pack_codes(c.data_ptr<int8_t>(), c.stride(0), reinterpret_cast<uint32_t*>(out.data_ptr()), K, N,
+                             (int)max_bits, cur_stream(c)),
+           "pack_codes");
+  return out;
+}
+
+// unpack (grinqh/utils.py:149-177): [K, (b/2)*N/16] -> [K, N] uint8 (shifted code >> (8-b))
+at::Tensor unpack(const at::Tensor& packed, int64_t max_bits, int64_t original_n) {
+  check_cuda(packed, "packed");
+  TORCH_CHECK(is_word32(packed) && packed.dim() == 2, "GRINQH unpack: expects a 2-D uint32/int32 tensor");
+  const at::Tensor p = packed.contiguous();
+  const int64_t K = p.size(0), N = original_n * 4;
+  TORCH_CHECK(p.size(1) >= (max_bits / 2) * (N / 16), "GRINQH unpack: packed tensor too narrow");
+  TORCH_CHECK(p.size(1) == (max_bits / 2) * (N / 16), "GRINQH unpack: packed width does not match max_bits/original_n");
+  const c10::cuda::CUDAGuard guard(p.device());
+  at::Tensor out = at::empty({K, N}, p.options().dtype(at::kByte));
+  check_ok(grinqh_unpack(reinterpret_cast<const uint32_t*>(p.data_ptr()), out.data_ptr<uint8_t>(), K, N, (int)max_bits,
+                         cur_stream(p)),
+           "unpack");
+  return out;
+}
+
+// grade (grinqh/kernel.py:100-116): per-element zone masks and their union over rows
+std::tuple<at::Tensor, at::Tensor> grade(const at::Tensor& x, at::ArrayRef<double> thresholds, int64_t max_bits) {
+  check_cuda(x, "x");
+  const int dt = dtype_code(x, "x");
+  const at::Tensor xf = x.reshape({-1, x.size(-1)}).contiguous();
+  const int64_t M = xf.size(0), K = xf.size(1);
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor masks = at::empty({M, K}, x.options().dtype(at::kByte));
+  at::Tensor uni = at::empty({K}, x.options().dtype(at::kByte));
+  const auto th = thresholds4(thresholds);
+  check_ok(grinqh_grade(xf.data_ptr(), dt, M, K, th.data(), (int)max_bits, masks.data_ptr<uint8_t>(),
+                        uni.data_ptr<uint8_t>(), cur_stream(x)),
+           "grade");
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  return {masks.view(shape), uni};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(grinqh, m) {
+  m.def("gemm_or_gemv(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
+        "int group_size, int original_n, float[] thresholds, bool use_marlin=False) -> Tensor");
+  m.def("linear(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
+        "int group_size, int original_n, float[] thresholds, int mode) -> Tensor");
+  m.def("pack(Tensor words, int max_bits) -> Tensor");
+  m.def("pack_codes(Tensor codes, int max_bits) -> Tensor");
+  m.def("unpack(Tensor packed, int max_bits, int original_n) -> Tensor");
+  m.def("grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
+  m.impl("gemm_or_gemv", &gemm_or_gemv);
+  m.impl("linear", &linear);
+  m.impl("pack", &pack);
+  m.impl("pack_codes", &pack_codes);
+  m.impl("unpack", &unpack);
+  m.impl("grade", &grade);
+}
