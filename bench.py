@@ -1,0 +1,433 @@
+#!/usr/bin/env python
+"""GRINQH quantized-linear benchmark (B200, sm_100a).
+
+Workload (configs[1] of the baseline, Llama-3-8B linear shapes): one decoder
+layer's four quantized linears -- qkv 4096->6144, o 4096->4096, gate_up
+4096->28672, down 14336->4096 -- b = 8 bit weights in bit planes, group 128, bf16
+activations. A *step* is one pass of the hot path over one batch: the four linears
+at the decode batch M (default 1: the graded GEMV, thresholds = quantiles
+.2/.4/.6/.8 of a 512-token calibration batch).
+
+Metric: algorithmic HBM bytes / second over the whole job (weight planes the
+grades select + scales of touched groups + activations + outputs). Two copies of
+the layer's weights are rotated (436 MB at b=8 > 126 MB L2), so every step reads
+its weights from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); each rank runs the same workload on
+its own GPU with no collective on the data path (replicas, weak scaling); the
+time is the max over ranks and the value sums all ranks' bytes.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "vllm-grinqh-plugin_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+SHAPES = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 28672), "down": (14336, 4096)}
+GROUP = 128
+QUANTILES = [0.2, 0.4, 0.6, 0.8]
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- data
+def make_layer(dev, bits, seed):
+    """RTN-quantized N(0, 0.02) weights -> bit planes; bf16 scales (synthetic)."""
+    from grinqh.utils import pack_codes
+    g = torch.Generator(device=dev).manual_seed(seed)
+    qmax = (1 << (bits - 1)) - 1
+    layer = {}
+    for name, (K, N) in SHAPES.items():
+        w = torch.randn((K, N), generator=g, device=dev) * 0.02
+        s = (w.view(K // GROUP, GROUP, N).abs().amax(1) / qmax).clamp_min(1e-8).to(torch.bfloat16)
+        codes = torch.clamp(torch.round(w / s.float().repeat_interleave(GROUP, 0)), -qmax - 1, qmax).to(torch.int8)
+        layer[name] = (pack_codes(codes, bits), s)
+        del w, codes
+    return layer
+
+
+def make_inputs(dev, M, seed):
+    """bf16 N(0,1) activations, 1% fixed outlier channels x20; thresholds from a
+    seeded 512-token calibration batch of the same distribution."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    xs, ths = {}, {}
+    for name, (K, N) in SHAPES.items():
+        idx = torch.randperm(K, generator=g, device=dev)[: max(1, K // 100)]
+        x = torch.randn((M, K), generator=g, device=dev)
+        x[:, idx] *= 20
+        cal = torch.randn((512, K), generator=g, device=dev)
+        cal[:, idx] *= 20
+        a = cal.to(torch.bfloat16).abs().float().flatten()
+        # torch.quantile is limited to 16M elements: sort-based linear interpolation
+        srt = torch.sort(a).values
+        th = []
+        for q in QUANTILES:
+            pos = q * (srt.numel() - 1)
+            lo = int(math.floor(pos))
+            hi = min(lo + 1, srt.numel() - 1)
+            th.append(float(srt[lo] + (srt[hi] - srt[lo]) * (pos - lo)))
+        xs[name] = x.to(torch.bfloat16)
+        ths[name] = th
+    return xs, ths
+
+
+def algorithmic_bytes(xs, ths, bits, M, graded):
+    """Bytes one step must move: active planes (union over rows) + touched scale
+    groups + x + y, per linear (roofline definition of the hot path)."""
+    from grinqh.kernel import grinqh_grade
+    per = {}
+    for name, (K, N) in SHAPES.items():
+        if graded:
+            _, uni = grinqh_grade(xs[name], ths[name], bits)
+            u = uni.to(torch.int32)
+            planes = int(sum(((u >> z) & 1).sum().item() for z in range(bits // 2)))
+            groups = int((uni.view(K // GROUP, GROUP) != 0).any(1).sum().item())
+        else:
+            planes, groups = K * (bits // 2), K // GROUP
+        per[name] = planes * (N // 4) + groups * N * 2 + 2 * M * K + 2 * M * N
+    return per
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons (read-only queries)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap", 0x1: "gpu_idle"}
+
+    def __init__(self, index):
+        self.samples, self.ok = [], False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                try:
+                    rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    rs = self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self, t0, t1):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-3:]
+        reasons = set()
+        for _, _, rs in inside:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(inside)}
+
+
+# ----------------------------------------------------------------------------- ours
+def run_ours(args, rank, world, dev):
+    from grinqh.kernel import grinqh_gemm_or_gemv, grinqh_linear, MODE_DENSE
+    bits, M = args.bits, args.m
+    torch.cuda.set_device(dev)
+    layers = [make_layer(dev, bits, 1000 * rank + s) for s in range(2)]  # 2 copies > L2
+    xs, ths = make_inputs(dev, M, 7 + rank)
+    graded = M == 1
+    per = algorithmic_bytes(xs, ths, bits, M, graded)
+    step_bytes = sum(per.values())
+
+    def step(layer, xin):
+        outs = []
+        for name, (K, N) in SHAPES.items():
+            w, s = layer[name]
+            outs.append(grinqh_gemm_or_gemv(xin[name], w, s, None, bits, GROUP, N // 4, ths[name]))
+        return outs
+
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize(dev)
+    # CUDA graphs: one graph per weight copy holding G steps (the op is capturable:
+    # no host sync, workspace from the caching allocator)
+    G = 8
+    graphs = []
+    with torch.cuda.stream(stream):
+        for _ in range(3):  # warm the allocator / lazy init before capture
+            step(layers[0], xs)
+        torch.cuda.synchronize(dev)
+        for li in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(G):
+                    step(layers[li], xs)
+            graphs.append(g)
+    torch.cuda.synchronize(dev)
+
+    def replay(nsteps):
+        full, rem = divmod(nsteps, G)
+        for i in range(full):
+            graphs[i % 2].replay()
+        for i in range(rem):  # remainder steps eagerly on the same stream
+            step(layers[(full + i) % 2], xs)
+
+    with torch.cuda.stream(stream):
+        replay(max(args.warmup, 3))
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(dev.index if dev.index is not None else 0).start()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_host0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        replay(args.steps)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_host1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = step_bytes * args.steps * world
+    value = total_bytes / (ms / 1e3) / 1e9
+
+    # ---- dominant kernel (gate_up) alone: average launch duration, rotating 2 copies
+    name = "gate_up"
+    K, N = SHAPES[name]
+    R = 64
+    with torch.cuda.stream(stream):
+        gk = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gk, stream=stream):
+            for i in range(R):
+                w, s = layers[i % 2][name]
+                grinqh_gemm_or_gemv(xs[name], w, s, None, bits, GROUP, N // 4, ths[name])
+        gk.replay()
+        torch.cuda.synchronize(dev)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(5):
+            gk.replay()
+        k1.record(stream)
+    torch.cuda.synchronize(dev)
+    kern_ms = k0.elapsed_time(k1) / (5 * R)
+    hbm_peak, tc_peak, peak_src = _peaks()
+    achieved = per[name] / (kern_ms / 1e3) / 1e9
+
+    # ---- end to end through the public op with host buffers: pinned H2D of each
+    # step's activations, the four linears, D2H of the outputs, per step
+    host_x = {n: xs[n].cpu().pin_memory() for n in SHAPES}
+    host_y = {n: torch.empty((M, SHAPES[n][1]), dtype=torch.bfloat16).pin_memory() for n in SHAPES}
+    dev_x = {n: torch.empty_like(xs[n]) for n in SHAPES}
+    h2d = sum(t.numel() * t.element_size() for t in host_x.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_y.values())
+
+    def e2e_step(li):
+        for n in SHAPES:
+            dev_x[n].copy_(host_x[n], non_blocking=True)
+        outs = step(layers[li], dev_x)
+        for n, o in zip(SHAPES, outs):
+            host_y[n].copy_(o, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        ge = []
+        for li in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                e2e_step(li)
+            ge.append(g)
+        for i in range(3):
+            ge[i % 2].replay()
+        torch.cuda.synchronize(dev)
+        n_e2e = max(20, min(args.steps, 200))
+        t_e = 0.0
+        for i in range(n_e2e):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ge[i % 2].replay()
+            b.record(stream)
+            b.synchronize()  # the host reads the step's result
+            t_e += a.elapsed_time(b)
+    e2e_ms = t_e / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = step_bytes * world / (e2e_ms / 1e3) / 1e9
+
+    line = {
+        "metric": "quant-linear HBM GB/s, Llama-3-8B layer linears (qkv+o+gate_up+down), decode",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 6), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"configs[1] Llama-3-8B linear shapes, M={M} "
+                               f"{'graded GEMV (quantile .2/.4/.6/.8 thresholds)' if graded else 'dense'}, "
+                               f"b={bits}, group {GROUP}",
+                   "shapes": {k: list(v) for k, v in SHAPES.items()}, "M": M, "max_bits": bits,
+                   "group_size": GROUP, "algorithmic_bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2: two weight copies rotated (%.0f MB per copy)" %
+                         (sum(w.numel() * 4 + s.numel() * 2 for w, s in layers[0].values()) / 1e6),
+                   "parallelism": f"replicas x{world} (no collective on the data path)",
+                   "timing": "CUDA events around CUDA-graph replays of the K steps"},
+        "roofline": {"bound": "hbm", "kernel": f"{name} graded GEMV" if graded else f"{name} dense",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+                     "bytes_per_launch": per[name], "avg_launch_us": round(kern_ms * 1e3, 3),
+                     "traffic": None},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(t_host0, t_host1),
+        "per_linear_bytes": per,
+    }
+    return line
+
+
+# ----------------------------------------------------------------------------- reference (CPU)
+def _cpu_reference(args, steps_to_time, threads):
+    """The reference's CPU path (restated with torch CPU ops in oracle/cpu_path.py) on
+    the same workload: per step the four linears at M rows."""
+    import oracle.cpu_path as CP
+    from oracle import grinqh_oracle as O
+    torch.set_num_threads(threads)
+    bits, M = args.bits, args.m
+    rng = np.random.default_rng(0)
+    layer = {}
+    for name, (K, N) in SHAPES.items():
+        codes = rng.integers(-(1 << (bits - 1)), 1 << (bits - 1), size=(K, N)).astype(np.int8)
+        packed = torch.from_numpy(O.pack_codes(codes, bits).view(np.int32))
+        s = (torch.rand((K // GROUP, N)) * 1e-3).to(torch.bfloat16)
+        x = torch.randn((M, K)).to(torch.bfloat16)
+        th = torch.quantile(x.abs().float().flatten(), torch.tensor(QUANTILES)).tolist()
+        layer[name] = (packed, s, x, th)
+    total_bytes = 0
+    for name, (K, N) in SHAPES.items():
+        packed, s, x, th = layer[name]
+        if M == 1:
+            m = O.grade(x.float().numpy()[0], th, bits)
+            planes = int(sum(((m >> z) & 1).sum() for z in range(bits // 2)))
+            groups = int((m.reshape(K // GROUP, GROUP) != 0).any(1).sum())
+        else:
+            planes, groups = K * (bits // 2), K // GROUP
+        total_bytes += planes * (N // 4) + groups * N * 2 + 2 * M * K + 2 * M * N
+
+    def step():
+        for name, (K, N) in SHAPES.items():
+            packed, s, x, th = layer[name]
+            CP.linear(x, packed, s, bits, GROUP, N // 4, th)
+
+    step()  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps_to_time):
+        step()
+    dt = (time.perf_counter() - t0) / steps_to_time
+    return total_bytes / dt / 1e9, dt, total_bytes
+
+
+def run_reference(args):
+    threads = os.cpu_count() or 1
+    steps = max(1, min(args.steps, 3))
+    gbs, dt, nbytes = _cpu_reference(args, steps, threads)
+    return {
+        "impl": "reference",
+        "metric": "quant-linear HBM GB/s, Llama-3-8B layer linears (qkv+o+gate_up+down), decode",
+        "value": round(gbs, 4), "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": 1,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"configs[1] Llama-3-8B linear shapes, M={args.m}, b={args.bits}, group {GROUP}",
+                   "algorithmic_bytes_per_step": nbytes,
+                   "path": "reference CPU path restated in torch (oracle/cpu_path.py): M==1 masked-weight "
+                           "oracle + fp32 matmul, M>1 eager dequant + matmul"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{steps} full step(s) of the workload"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=1, help="decode batch rows per linear")
+    ap.add_argument("--bits", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    line = run_ours(args, rank, world, dev)
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            gbs, dt, _ = _cpu_reference(args, 1, threads)
+            line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                                    "sample": "1 full step of the workload (4 linears) on the host cores, "
+                                              "reference CPU path restated in torch (oracle/cpu_path.py)"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

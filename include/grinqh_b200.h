@@ -72,6 +72,12 @@ int grinqh_abi_version(void);
 const char *grinqh_status_string(int status);
 const char *grinqh_last_error(void);
 
+/* Number of pipeline waits (mbarrier) in this library's kernels on the current
+ * device that hit their iteration limit since the last call, then reset to 0.
+ * Non-zero means a kernel gave up waiting and its output is not valid. Synchronous.
+ * (No reference counterpart: the reference's Triton kernels have no device waits.) */
+int grinqh_take_error_flags(unsigned *timeouts);
+
 /* Bit-plane pack of already preshuffled and shifted code words.
  * words_dev [K, n_words] uint32 (4 code bytes per word, codes in the MSBs),
  * n_words % 4 == 0; out_dev [K, (b/2)*n_words/4] uint32.
@@ -97,8 +103,8 @@ int grinqh_grade(const void *x_dev, int dtype, int64_t M, int64_t K, const float
                  int max_bits, uint8_t *masks_dev, uint8_t *union_dev, grinqh_stream_t stream);
 
 /* Scratch bytes grinqh_gemm_or_gemv / grinqh_gemv_batch_union / grinqh_prefill_gemm
- * need for these sizes and mode (0 is possible). */
-size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int mode);
+ * need for these sizes, group size and mode (0 is possible). Host-only. */
+size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int group_size, int mode);
 
 /* The quantized linear y = x @ W (+ bias), torch.ops.grinqh.gemm_or_gemv
  * (grinqh/kernel.py:646-710). workspace_dev: grinqh_workspace_size() bytes,

@@ -41,10 +41,10 @@ def test_workspace_size_is_host_only():
     from grinqh import _ext
     lib = _ext.cabi()
     # K split over several CTAs -> fp32 partials + tickets
-    ws = lib.grinqh_workspace_size(1, 4096, 4096, 8, _ext.MODE_AUTO)
+    ws = lib.grinqh_workspace_size(1, 4096, 4096, 8, 128, _ext.MODE_AUTO)
     assert ws >= 4096 * 4 * 2
-    assert lib.grinqh_workspace_size(0, 4096, 4096, 8, _ext.MODE_AUTO) == 0
-    assert lib.grinqh_workspace_size(1, 4096, 4096, 8, 17) == 0  # unknown mode
+    assert lib.grinqh_workspace_size(0, 4096, 4096, 8, 128, _ext.MODE_AUTO) == 0
+    assert lib.grinqh_workspace_size(1, 4096, 4096, 8, 128, 17) == 0  # unknown mode
 
 
 def test_calls_without_gpu_fail_loudly():

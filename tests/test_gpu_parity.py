@@ -310,3 +310,12 @@ def test_scaling_and_determinism_at_full_size(M):
     if M == 1:
         z = grinqh_gemm_or_gemv(x, w, s, None, b, 128, N // 4, [1e30] * 4)
         assert torch.count_nonzero(z) == 0
+
+
+def test_no_pipeline_wait_timed_out():
+    """Every bounded mbarrier wait in the kernels run so far completed in time."""
+    import ctypes
+    from grinqh import _ext
+    v = ctypes.c_uint(123)
+    assert _ext.cabi().grinqh_take_error_flags(ctypes.byref(v)) == 0
+    assert v.value == 0

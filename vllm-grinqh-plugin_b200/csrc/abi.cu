@@ -3,6 +3,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "decode_m1.cuh"
 
 namespace grinqh {
 
@@ -77,6 +78,16 @@ static size_t workspace_for(const DecodePlan& p) {
   return align_up(p.partial_bytes, 256) + align_up(p.counter_bytes, 256);
 }
 
+static size_t workspace_for(const M1Plan& p) {
+  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
+}
+
+// Kernel choice: graded / union rows of one token use the register-streaming
+// single-row kernel; everything else the generic small-M kernel.
+static bool use_m1(int kmode, int64_t M, int64_t K, int64_t N, int group) {
+  return (kmode == kModeGraded || kmode == kModeUnion) && m1_supported(M, K, N, group);
+}
+
 static int validate(const void* x, int dtype, int64_t M, int64_t K, const void* w, const void* s, int bits,
                     int group, int64_t N, const void* y) {
   if (!valid_bits(bits)) return set_error(GRINQH_ERR_UNSUPPORTED, "max_bits must be 2, 4, 6 or 8 (got %d)", bits);
@@ -111,13 +122,14 @@ extern "C" const char* grinqh_status_string(int status) {
 
 extern "C" const char* grinqh_last_error(void) { return g_last_error.c_str(); }
 
-extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int mode) {
-  (void)max_bits;
+extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int group_size, int mode) {
+  if (group_size <= 0 || !valid_bits(max_bits)) return 0;
   const int km = resolve_mode(mode, M);
   if (km < 0 || M <= 0 || K <= 0 || N <= 0) return 0;
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
+  if (use_m1(km, M, K, N, group_size)) return workspace_for(plan_m1(K, N, group_size, sms));
   return workspace_for(plan_decode(M, K, N, km, sms));
 }
 
@@ -132,6 +144,34 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   GRINQH_REQUIRE(km >= 0, "unknown mode %d", mode);
   GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
   if (M == 0) return GRINQH_OK;
+
+  if (use_m1(km, M, K, N, group)) {
+    const M1Plan plan = plan_m1(K, N, group, sms);
+    const size_t need = workspace_for(plan);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
+    M1Args g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    g.rows_per_warp = plan.rows_per_warp;
+    g.rows_per_cta = plan.rows_per_cta;
+    for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
+    if (need > 0) {
+      char* base = static_cast<char*>(workspace);
+      g.slots = reinterpret_cast<float*>(base);
+      g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
+      const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
+      if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    return launch_m1(g, plan, dtype, max_bits / 2, stream);
+  }
 
   const DecodePlan plan = plan_decode(M, K, N, km, sms);
   const size_t need = workspace_for(plan);
@@ -160,6 +200,13 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   }
   return launch_decode(a, plan, km, dtype, max_bits / 2, stream);
+}
+
+extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
+  GRINQH_RETURN_IF(check_device());
+  const unsigned v = 0;  // no kernel in this build waits on an mbarrier
+  if (timeouts) *timeouts = v;
+  return GRINQH_OK;
 }
 
 extern "C" int grinqh_gemv_batch_union(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,

@@ -1,0 +1,39 @@
+// Host-side interface of the single-row graded GEMV (decode_m1.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace grinqh {
+
+struct M1Args {
+  const void* x;        // [K] dtype
+  const uint32_t* w;    // [K, nz*N/16] packed planes
+  const void* s;        // [K/group, N] dtype
+  const void* bias;     // [N] dtype or null
+  void* y;              // [N] dtype
+  float* slots;         // [tiles, clusters per tile, 512] fp32 (several clusters per tile)
+  unsigned* counters;   // [tiles] tickets; zero before the first launch, left zero
+  int K, N, group, rows_per_warp, rows_per_cta;
+  float t[4];
+};
+
+struct M1Plan {
+  int tiles, rows_per_warp, rows_per_cta, cluster, grid_splits;
+  size_t slot_bytes, counter_bytes, smem_bytes;
+};
+
+// staged per-row metadata (x, bias*x, grade), 16 bytes a row; aliased by the
+// 8 x 512 fp32 warp-reduction buffer after the main loop
+__host__ __device__ inline size_t m1_meta_bytes(int rows_per_cta) {
+  const size_t meta = (size_t)rows_per_cta * 16;
+  const size_t red = 8 * 512 * 4;
+  return meta > red ? meta : red;
+}
+
+bool m1_supported(int64_t M, int64_t K, int64_t N, int group);
+M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
+int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st);
+
+}  // namespace grinqh

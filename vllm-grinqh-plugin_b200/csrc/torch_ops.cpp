@@ -95,7 +95,7 @@ at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, cons
   at::Tensor y = at::empty({M, N}, x.options());
   if (M == 0) return y.view(out_shape);
   const auto th = thresholds4(thresholds);
-  const size_t ws_bytes = grinqh_workspace_size(M, K, N, (int)max_bits, mode);
+  const size_t ws_bytes = grinqh_workspace_size(M, K, N, (int)max_bits, (int)group_size, mode);
   at::Tensor ws;
   if (ws_bytes) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
   const int st = grinqh_gemm_or_gemv(xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()),

@@ -27,11 +27,12 @@ SIGNATURES = {
     "grinqh_abi_version": (_int, []),
     "grinqh_status_string": (ctypes.c_char_p, [_int]),
     "grinqh_last_error": (ctypes.c_char_p, []),
+    "grinqh_take_error_flags": (_int, [_ptr]),
     "grinqh_pack_words": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_pack_codes": (_int, [_ptr, _i64, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_unpack": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_grade": (_int, [_ptr, _int, _i64, _i64, _fptr, _int, _ptr, _ptr, _ptr]),
-    "grinqh_workspace_size": (_size, [_i64, _i64, _i64, _int, _int]),
+    "grinqh_workspace_size": (_size, [_i64, _i64, _i64, _int, _int, _int]),
     "grinqh_gemm_or_gemv": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr, _int,
                                    _ptr, _ptr, _size, _ptr]),
     "grinqh_gemv_batch_union": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr,
