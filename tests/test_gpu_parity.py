@@ -319,3 +319,27 @@ def test_no_pipeline_wait_timed_out():
     v = ctypes.c_uint(123)
     assert _ext.cabi().grinqh_take_error_flags(ctypes.byref(v)) == 0
     assert v.value == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 256, 256), (300, 384, 320), (512, 1024, 4096), (256, 4096, 6144)])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("b", [8, 4, 2, 6])
+def test_dense_tensor_core_gemm(M, K, N, dtype, b):
+    """Rows >= 64 run the tcgen05 GEMM (in-kernel dequant to dtype(w*s)); vs the oracle,
+    including a row tail (300), a column tail (N/16 = 20 words) and multiple tiles."""
+    from grinqh.kernel import grinqh_gemm_or_gemv
+    from grinqh.utils import pack_codes
+    rng = np.random.default_rng(M + K + N + b)
+    lim = 1 << (b - 1)
+    codes = rng.integers(-lim, lim, size=(K, N)).astype(np.int8)
+    s32 = (rng.random((K // 128, N)) * 0.02 + 0.001).astype(np.float32)
+    s_store = O.round_to_dtype(s32, dtype)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    xs = O.round_to_dtype(x, dtype)
+    bias = O.round_to_dtype(rng.standard_normal(N).astype(np.float32), dtype)
+    w = pack_codes(torch.from_numpy(codes).cuda(), b)
+    y = grinqh_gemm_or_gemv(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128,
+                            N // 4, [0.0] * 4)
+    ref = O.gemm_or_gemv(O.to_f32(xs, dtype), codes, O.to_f32(s_store, dtype), O.to_f32(bias, dtype), b, 128,
+                         [0.0] * 4, dtype)
+    assert_parity(f32(y), O.to_f32(ref, dtype))

@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "decode_m1.cuh"
+#include "gemm_tc.cuh"
 
 namespace grinqh {
 
@@ -82,8 +83,12 @@ static size_t workspace_for(const M1Plan& p) {
   return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
 }
 
+// Rows from which the dense path runs on the tensor cores (tcgen05 GEMM).
+constexpr int64_t kTcMinRows = 64;
+
 // Kernel choice: graded / union rows of one token use the register-streaming
-// single-row kernel; everything else the generic small-M kernel.
+// single-row kernel; dense rows >= kTcMinRows the tcgen05 GEMM; everything else
+// the generic small-M kernel.
 static bool use_m1(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return (kmode == kModeGraded || kmode == kModeUnion) && m1_supported(M, K, N, group);
 }
@@ -130,6 +135,7 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
   if (use_m1(km, M, K, N, group_size)) return workspace_for(plan_m1(K, N, group_size, sms));
+  if (km == kModeDense && M >= kTcMinRows && K % 64 == 0 && group_size % 64 == 0) return 0;  // tcgen05 GEMM
   return workspace_for(plan_decode(M, K, N, km, sms));
 }
 
@@ -173,6 +179,20 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_m1(g, plan, dtype, max_bits / 2, stream);
   }
 
+  if (km == kModeDense && M >= kTcMinRows && gemm_tc_supported(M, K, N, group, x, y)) {
+    GemmArgs g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.M = (int)M;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    return launch_gemm_tc(g, dtype, max_bits / 2, stream);
+  }
+
   const DecodePlan plan = plan_decode(M, K, N, km, sms);
   const size_t need = workspace_for(plan);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
@@ -204,7 +224,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
   GRINQH_RETURN_IF(check_device());
-  const unsigned v = 0;  // no kernel in this build waits on an mbarrier
+  const unsigned v = take_gemm_timeouts();
   if (timeouts) *timeouts = v;
   return GRINQH_OK;
 }
