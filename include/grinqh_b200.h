@@ -132,6 +132,30 @@ int grinqh_prefill_gemm(const void *x_dev, int dtype, int64_t M, int64_t K,
                         void *y_dev, void *workspace_dev, size_t workspace_bytes,
                         grinqh_stream_t stream);
 
+/* Single-row graded GEMV that allocates nothing (no counterpart in the reference,
+ * whose kernels always take their scratch from the torch allocator).
+ *
+ * For callers that cannot allocate device memory when they run the layer: code
+ * with a fixed memory budget reserved at start-up (embedded or real-time inference
+ * loops, plugin hosts that forbid allocation after initialisation) or hot paths
+ * that must not enter an allocator, which may synchronise the device or fail
+ * under fragmentation. Same computation as grinqh_gemm_or_gemv with M = 1 and
+ * mode GRINQH_MODE_AUTO (x [K], y [N]); the kernel's scratch lives in a 256 KiB
+ * device array inside this library instead of a caller workspace. Every GPU that
+ * loads the library holds that array until the process exits.
+ *   - The first call on a device looks up the array's device address (once per
+ *     device, with that device current); make that first call before any stream
+ *     capture.
+ *   - A launch plan whose scratch would exceed 256 KiB returns
+ *     GRINQH_ERR_WORKSPACE (the kernel's K split keeps every shape below it on a
+ *     148-SM B200, so this is a guard).
+ *   - All calls share the array: calls that can overlap on the GPU (different
+ *     streams, or graphs replayed concurrently) race and give wrong results;
+ *     serialise them, or use grinqh_gemm_or_gemv with separate workspaces. */
+int grinqh_gemv_noalloc(const void *x_dev, int dtype, int64_t K, const uint32_t *weight_packed_dev,
+                        const void *weight_scale_dev, const void *bias_dev, int max_bits, int group_size,
+                        int64_t N, const float *thresholds, void *y_dev, grinqh_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,7 @@ SIGNATURES = {
                                        _ptr, _ptr, _size, _ptr]),
     "grinqh_prefill_gemm": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _ptr, _ptr,
                                    _size, _ptr]),
+    "grinqh_gemv_noalloc": (_int, [_ptr, _int, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr, _ptr, _ptr]),
 }
 
 
