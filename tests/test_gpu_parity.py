@@ -41,6 +41,17 @@ def f32(t):
     return t.float().cpu().numpy()
 
 
+@pytest.fixture(params=["streaming", "tensor_cores"])
+def m1_kernel(request, monkeypatch):
+    """Runs a single-row test on both single-row kernels: the default register-
+    streaming one and the opt-in int8 tensor-core one (GRINQH_M1_TENSOR_CORES=1)."""
+    if request.param == "tensor_cores":
+        monkeypatch.setenv("GRINQH_M1_TENSOR_CORES", "1")
+    else:
+        monkeypatch.delenv("GRINQH_M1_TENSOR_CORES", raising=False)
+    return request.param
+
+
 def assert_parity(got, ref, max_rel=MAX_REL_TOL, fro=FRO_TOL):
     mx, fr = rel_errors(got, ref)
     assert mx <= max_rel and fr <= fro, f"max-rel {mx:.3e} (<= {max_rel}), fro {fr:.3e} (<= {fro})"
@@ -117,7 +128,7 @@ def test_grade_bit_exact(dtype, b):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("b", BITS)
 @pytest.mark.parametrize("q", ["spread", "all_or_nothing", "mild", "aggressive", "skip_all", "dense"])
-def test_graded_gemv_matches_reference(golden, dtype, b, q):
+def test_graded_gemv_matches_reference(golden, dtype, b, q, m1_kernel):
     """M == 1 graded GEMV vs the reference Triton kernel's output on identical inputs
     (tests/test_grinqh_ops.py:156-240 cases)."""
     from grinqh.kernel import grinqh_gemm_or_gemv
@@ -210,7 +221,7 @@ def _problem(rng, K, N, b, M, dtype="bf16", dist="normal"):
 
 @pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 6144), (14336, 4096)])
 @pytest.mark.parametrize("b", [8, 4])
-def test_llama_shapes_graded_m1(K, N, b):
+def test_llama_shapes_graded_m1(K, N, b, m1_kernel):
     from grinqh.kernel import grinqh_gemm_or_gemv
     from grinqh.utils import pack_codes
     rng = np.random.default_rng(K + N + b)

@@ -2,9 +2,12 @@
 #include <mutex>
 
 #include "common.cuh"
+
+#include <stdlib.h>
 #include "decode.cuh"
 #include "decode_m1.cuh"
 #include "gemm_tc.cuh"
+#include "decode_tc.cuh"
 
 namespace grinqh {
 
@@ -83,6 +86,20 @@ static size_t workspace_for(const M1Plan& p) {
   return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
 }
 
+static size_t workspace_for(const M1TcPlan& p) {
+  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
+}
+
+// The int8 tensor-core single-row kernel (decode_tc.cu) is selected only when
+// GRINQH_M1_TENSOR_CORES=1: it is exact but slower than the register-streaming
+// kernel on the Llama-3-8B shapes (gate_up 64 us vs 48 us at b = 8), so it is not
+// the default. The variable is read on every call (a getenv, no allocation).
+static bool use_m1tc(int kmode, int64_t M, int64_t K, int64_t N, int group) {
+  const char* e = getenv("GRINQH_M1_TENSOR_CORES");
+  if (!e || e[0] != '1') return false;
+  return (kmode == kModeGraded || kmode == kModeUnion) && m1tc_supported(M, K, N, group);
+}
+
 // Rows from which the dense path runs on the tensor cores (tcgen05 GEMM).
 constexpr int64_t kTcMinRows = 64;
 
@@ -134,6 +151,7 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
+  if (use_m1tc(km, M, K, N, group_size)) return workspace_for(plan_m1tc(K, N, sms));
   if (use_m1(km, M, K, N, group_size)) return workspace_for(plan_m1(K, N, group_size, sms));
   if (km == kModeDense && M >= kTcMinRows && K % 64 == 0 && group_size % 64 == 0) return 0;  // tcgen05 GEMM
   return workspace_for(plan_decode(M, K, N, km, sms));
@@ -150,6 +168,31 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   GRINQH_REQUIRE(km >= 0, "unknown mode %d", mode);
   GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
   if (M == 0) return GRINQH_OK;
+
+  if (use_m1tc(km, M, K, N, group)) {
+    const M1TcPlan plan = plan_m1tc(K, N, sms);
+    const size_t need = workspace_for(plan);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    M1TcArgs g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.tiles = plan.tiles;
+    g.units_per_cta = plan.units_per_cta;
+    for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
+    char* base = static_cast<char*>(workspace);
+    g.slots = reinterpret_cast<float*>(base);
+    g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
+    const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
+    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    return launch_m1tc(g, plan, dtype, max_bits / 2, stream);
+  }
 
   if (use_m1(km, M, K, N, group)) {
     const M1Plan plan = plan_m1(K, N, group, sms);
@@ -224,7 +267,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
   GRINQH_RETURN_IF(check_device());
-  const unsigned v = take_gemm_timeouts();
+  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts();
   if (timeouts) *timeouts = v;
   return GRINQH_OK;
 }

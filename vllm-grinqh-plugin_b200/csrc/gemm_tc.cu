@@ -162,12 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         for (int z = 0; z < 4; ++z) P[i][z] = (z < NZ && jvalid && q < nk) ? __ldcs(wr + (size_t)z * n16) : 0u;
       }
     };
-    load_planes(P1, 0);
-    load_planes(P2, 1);
     const int steps_per_group = a.group / BK;
     load_scales(sreg, 0);
     if (nk > steps_per_group) load_scales(snext, 1);
-    for (int q = 0; q < nk; ++q) {
+    auto convert_step = [&](const uint32_t (&Pc)[4][4], int q) {
       const int s = q % STAGES;
       if (q > 0 && q % steps_per_group == 0) {  // next K group: its scales were prefetched
         const int g = q / steps_per_group;
@@ -175,15 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         for (int c = 0; c < 16; ++c) sreg[c] = snext[c];
         if ((g + 1) * steps_per_group < nk) load_scales(snext, g + 1);
       }
-      uint32_t Pc[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int z = 0; z < 4; ++z) {
-          Pc[i][z] = P1[i][z];
-          P1[i][z] = P2[i][z];
-        }
-      load_planes(P2, q + 2);
       if (q >= STAGES) mbar_wait(&empty[s], ((q / STAGES) - 1) & 1);
       unsigned char* bst = sB + s * kStageB;
 #pragma unroll
@@ -208,6 +197,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       fence_proxy_async_smem();  // make the generic-proxy stores visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&b_full[s]);
+    };
+    // the plane buffers rotate by name: a register copy of a pending load would wait for it
+    load_planes(P1, 0);
+    load_planes(P2, 1);
+    for (int q = 0; q < nk; q += 2) {
+      convert_step(P1, q);
+      load_planes(P1, q + 2);
+      if (q + 1 < nk) {
+        convert_step(P2, q + 1);
+        load_planes(P2, q + 3);
+      }
     }
 
     // ------------------------------------------------------------ epilogue

@@ -63,7 +63,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wait for the phase with the given parity to complete. Gives up (records it and
 // returns false) after kWaitNs, or at once when another wait already gave up, so a
 // stalled pipeline ends the kernel quickly instead of hanging the GPU.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -98,6 +98,18 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t
 // (counts as one of the barrier's initial arrivals).
 __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------- predicated loads
+// v = (mask & bit) ? *p : 0, streaming (evict-first) global load
+__device__ __forceinline__ uint32_t ld_cs_if(const uint32_t* p, uint32_t mask, uint32_t bit) {
+  uint32_t v;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tand.b32 %0, %2, %3;\n\tsetp.ne.b32 q, %0, 0;\n\tmov.b32 %0, 0;\n\t"
+      "@q ld.global.cs.u32 %0, [%1];\n\t}"
+      : "=r"(v)
+      : "l"(p), "r"(mask), "r"(bit));
+  return v;
 }
 
 // ---------------------------------------------------------------- TMA (tensor)
@@ -170,6 +182,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+
+// 32 lanes x 4 consecutive 32-bit TMEM columns -> 4 registers per thread
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() {
