@@ -152,7 +152,13 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
   if (use_m1tc(km, M, K, N, group_size)) return workspace_for(plan_m1tc(K, N, sms));
-  if (use_m1(km, M, K, N, group_size)) return workspace_for(plan_m1(K, N, group_size, sms));
+  if (use_m1(km, M, K, N, group_size)) {
+    // a weight or scale view that is not 8 / 4-byte aligned runs the generic kernel,
+    // and this query does not see the pointers: cover both plans
+    const size_t a = workspace_for(plan_m1(K, N, group_size, sms));
+    const size_t b = workspace_for(plan_decode(M, K, N, km, sms));
+    return a > b ? a : b;
+  }
   if (km == kModeDense && M >= kTcMinRows && K % 64 == 0 && group_size % 64 == 0) return 0;  // tcgen05 GEMM
   return workspace_for(plan_decode(M, K, N, km, sms));
 }
@@ -194,7 +200,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_m1tc(g, plan, dtype, max_bits / 2, stream);
   }
 
-  if (use_m1(km, M, K, N, group)) {
+  if (use_m1(km, M, K, N, group) && m1_pointers_ok(w, s)) {
     const M1Plan plan = plan_m1(K, N, group, sms);
     const size_t need = workspace_for(plan);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))

@@ -1,19 +1,22 @@
 // Single-row graded GEMV (the reference's M == 1 path, grinqh/kernel.py:39-167)
 // streamed from HBM through registers.
 //
-// Tile: a warp owns 32 packed-word columns (one word = 16 output columns per lane,
-// 128 B per plane row) and a contiguous chunk of K rows; the 8 warps of a CTA take
-// consecutive chunks of the CTA's row range for the same 32 words. Each lane keeps
-// a D-deep ring of plane words in registers: while row r is merged and multiplied,
-// the active planes of row r + D are already in flight (a row graded 0 issues no
-// load), so a CTA keeps 8 * D * 4 * 128 B of weights in flight.
+// Tile: a CTA owns a slice of 64 packed words (1024 output columns); each lane owns
+// two neighbouring words and reads both with one 8-byte load per active plane, so a
+// warp reads 256 contiguous bytes of every plane row it needs. The 8 warps of a CTA
+// take consecutive chunks of the CTA's K range. Each warp grades its own rows into
+// shared memory (no CTA-wide barrier before the first weight load) and keeps a
+// kD-row ring of plane words in flight: while row r is merged and multiplied, the
+// active planes of row r + kD are already loading. A row graded 0 issues no load
+// and no arithmetic.
 //
 // Scales are applied per K group, s * (sum(code * x) + sum(bias * x)) as in
-// kernel.py:148-158. The 8 warps are summed in shared memory; up to 8 CTAs that
-// split the same tile along K form a thread-block cluster and rank 0 adds their
-// partials over distributed shared memory; when a tile has several clusters, their
-// sums go to fp32 slots and the last cluster leader (atomic ticket) adds them in
-// cluster order. Every sum has a fixed order, so results are deterministic.
+// kernel.py:148-158, at group boundaries and at the end of a chunk. The 8 warps are
+// summed in shared memory; up to 8 CTAs that split the same slice along K form a
+// thread-block cluster and rank 0 adds their partials over distributed shared
+// memory; when a slice has several clusters, their sums go to fp32 slots and the
+// last cluster leader (atomic ticket) adds them in cluster order. Every sum has a
+// fixed order, so results are deterministic.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -26,8 +29,10 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kTileJ = 32;
-constexpr int kTileN = 16 * kTileJ;
+constexpr int kWpl = 2;                // packed words per lane
+constexpr int kSliceW = 32 * kWpl;     // words per slice
+constexpr int kSliceN = 16 * kSliceW;  // output columns per slice
+constexpr int kD = 4;                  // rows in flight per warp
 
 struct RowMeta {
   float x, bx;
@@ -46,9 +51,9 @@ __device__ __forceinline__ int zone_bias(uint32_t m) {
   return v;
 }
 
-// acc[p]: columns c = 2p, 2p+1 of the lane's packed word (c = 4i + L)
+// acc[p]: columns c = 2p, 2p+1 of one packed word (c = 4i + L)
 __device__ __forceinline__ void fma_word(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, float2 xv,
-                                         float2 (&acc)[8]) {
+                                         float2* acc) {
   uint32_t q[4];
   merge_planes(a0 ^ kSignFlip, a1, a2, a3, q);
   const float2 magic = make_float2(-8388736.0f, -8388736.0f);
@@ -63,109 +68,156 @@ __device__ __forceinline__ void fma_word(uint32_t a0, uint32_t a1, uint32_t a2, 
   }
 }
 
-template <int NZ, int D, typename T>
-__global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
+// The active planes of one row for this lane's two words: P[z] = plane z words
+// (zero when the row's grade does not include zone z).
+template <int NZ>
+__device__ __forceinline__ void load_row(uint2 (&P)[4], const uint32_t* wr, uint32_t m, uint32_t pstride) {
+#pragma unroll
+  for (int z = 0; z < 4; ++z) {
+    P[z] = make_uint2(0u, 0u);
+    if (z < NZ && (m & (1u << z))) P[z] = __ldcs(reinterpret_cast<const uint2*>(wr + (size_t)z * pstride));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float2 scale2(uint32_t bits);
+template <>
+__device__ __forceinline__ float2 scale2<__nv_bfloat16>(uint32_t bits) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bits));
+}
+template <>
+__device__ __forceinline__ float2 scale2<__half>(uint32_t bits) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&bits));
+}
+
+// Rows [kb, ke) of slice `tile` for this warp: grade them, stream their planes and
+// add s * partial sums into this lane's 32 columns of wacc (kernel.py:100-158).
+template <int NZ, typename T>
+__device__ __forceinline__ void warp_chunk(const M1Args& a, int tile, int kb, int ke, RowMeta* wrows,
+                                           float* wacc) {
   constexpr int kShift = 8 - 2 * NZ;
   constexpr float kInvShift = 1.0f / float(1 << kShift);
+  const int lane = threadIdx.x & 31;
+  const int n16 = a.N >> 4;
+  const int j0 = tile * kSliceW + kWpl * lane;  // this lane's first word (n16 is even)
+  const bool jvalid = j0 < n16;
+  const T* x = static_cast<const T*>(a.x);
+  const uint32_t pstride = (uint32_t)n16;
+  const size_t row_words = (size_t)NZ * n16;
+  const int n = ke - kb;  // a multiple of kD (chunk bounds, K and the group size are)
+
+  // grade (kernel.py:100-116): fp32 |x| > t_z, bias * x
+  for (int i = lane; i < n; i += 32) {
+    const float xv = Act<T>::to_f(x[kb + i]);
+    const float ax = fabsf(xv);
+    uint32_t g = (uint32_t)(ax > a.t[0]) | ((uint32_t)(ax > a.t[1]) << 1) | ((uint32_t)(ax > a.t[2]) << 2) |
+                 ((uint32_t)(ax > a.t[3]) << 3);
+    g &= (1u << NZ) - 1u;
+    wrows[i] = RowMeta{xv, float(zone_bias<NZ>(g)) * xv, g, 0u};
+  }
+  __syncwarp();
+  if (n <= 0) return;
+
+  float2 gacc[16];
+#pragma unroll
+  for (int p = 0; p < 16; ++p) gacc[p] = make_float2(0.f, 0.f);
+  float bsum = 0.f;
+  const uint32_t* wr = a.w + (size_t)kb * row_words + (jvalid ? j0 : 0);
+  int g = kb / a.group;
+  int next_group_k = (g + 1) * a.group;
+  // scales of the current group as packed dtype pairs: s[g, c * n16 + j0 .. j0 + 1]
+  uint32_t sv[16];
+  auto load_scales = [&](int gi) {
+    const uint32_t* sp =
+        reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.s) + (size_t)gi * a.N + (jvalid ? j0 : 0));
+#pragma unroll
+    for (int c = 0; c < 16; ++c) sv[c] = __ldg(sp + (size_t)c * (n16 >> 1));
+  };
+  load_scales(g);
+  // wacc += s * (sum(code * x) / 2^shift + sum(bias * x)) for the finished group
+  auto flush = [&]() {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      // gacc[h * 8 + p] holds word h, columns 2p, 2p+1
+      const int p = c >> 1;
+      const float w0 = (c & 1) ? gacc[p].y : gacc[p].x;
+      const float w1 = (c & 1) ? gacc[8 + p].y : gacc[8 + p].x;
+      const float2 s2 = scale2<T>(sv[c]);
+      float2* dst = reinterpret_cast<float2*>(wacc + c * kSliceW);
+      float2 v = *dst;
+      v.x = fmaf(s2.x, fmaf(w0, kInvShift, bsum), v.x);
+      v.y = fmaf(s2.y, fmaf(w1, kInvShift, bsum), v.y);
+      *dst = v;
+    }
+#pragma unroll
+    for (int p = 0; p < 16; ++p) gacc[p] = make_float2(0.f, 0.f);
+    bsum = 0.f;
+  };
+
+  // lanes past the last word load nothing (their grades read as 0)
+  const uint32_t lmask = jvalid ? 0xFu : 0u;
+  uint2 P0[4], P1[4], P2[4], P3[4];
+  load_row<NZ>(P0, wr, wrows[0].m & lmask, pstride);
+  load_row<NZ>(P1, wr + row_words, wrows[1].m & lmask, pstride);
+  load_row<NZ>(P2, wr + 2 * row_words, wrows[2].m & lmask, pstride);
+  load_row<NZ>(P3, wr + 3 * row_words, wrows[3].m & lmask, pstride);
+  const uint32_t* wn = wr + kD * row_words;  // plane words of row i + kD
+
+  auto step = [&](uint2 (&P)[4], int i) {
+    const RowMeta rm = wrows[i];
+    bsum += rm.bx;
+    if (rm.m) {
+      const float2 xv = make_float2(rm.x, rm.x);
+      fma_word(P[0].x, P[1].x, P[2].x, P[3].x, xv, gacc);
+      fma_word(P[0].y, P[1].y, P[2].y, P[3].y, xv, gacc + 8);
+    }
+    load_row<NZ>(P, wn, i + kD < n ? (wrows[i + kD].m & lmask) : 0u, pstride);
+    wn += row_words;
+  };
+
+  // a block of kD rows never straddles a group (kb and the group size are multiples of kD)
+  for (int i = 0; i < n; i += kD) {
+    if (kb + i == next_group_k) {  // K group boundary: apply the finished group's scales
+      flush();
+      next_group_k += a.group;
+      load_scales(++g);
+    }
+    step(P0, i);
+    step(P1, i + 1);
+    step(P2, i + 2);
+    step(P3, i + 3);
+  }
+  flush();
+}
+
+template <int NZ, typename T>
+__global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  RowMeta* rows = reinterpret_cast<RowMeta*>(smem);                       // staged rows of the CTA
-  float* red = reinterpret_cast<float*>(smem);                            // aliases rows after the loop
-  float* part = reinterpret_cast<float*>(smem + m1_meta_bytes(a.rows_per_cta));  // CTA partial (DSMEM)
+  RowMeta* rows = reinterpret_cast<RowMeta*>(smem);  // staged rows of the CTA
+  // per-warp scaled accumulators [warp][column], column = c * kSliceW + word; they
+  // are also the buffer the 8 warps are summed from
+  float* red = reinterpret_cast<float*>(smem + m1_meta_bytes(a.rows_per_cta));
+  float* part = red + kWarps * kSliceN;  // CTA partial (read by the cluster over DSMEM)
   __shared__ int s_last;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
   const int n16 = a.N >> 4;
-  const int jw = tile * kTileJ + lane;
-  const bool jvalid = jw < n16;
   const int k0 = split * a.rows_per_cta;
-  const int k1 = min(k0 + a.rows_per_cta, a.K);
-  const int nrows = max(0, k1 - k0);
-  const T* x = static_cast<const T*>(a.x);
-  const T* sc = static_cast<const T*>(a.s);
-  const size_t row_words = (size_t)NZ * n16;
+  const int rb = min(a.K, k0 + warp * a.rows_per_warp);
+  const int re = min(a.K, rb + a.rows_per_warp);
+  float* wacc = red + warp * kSliceN + kWpl * lane;  // this lane's columns: wacc[c * kSliceW + h]
+#pragma unroll
+  for (int c = 0; c < 16; ++c) *reinterpret_cast<float2*>(wacc + c * kSliceW) = make_float2(0.f, 0.f);
+  warp_chunk<NZ, T>(a, tile, rb, re, rows + (rb - k0), wacc);
 
-  // grade the CTA's rows once (kernel.py:100-116): fp32 |x| > t_z, bias * x
-  for (int i = threadIdx.x; i < nrows; i += kThreads) {
-    const float xv = Act<T>::to_f(x[k0 + i]);
-    const float ax = fabsf(xv);
-    uint32_t g = (uint32_t)(ax > a.t[0]) | ((uint32_t)(ax > a.t[1]) << 1) | ((uint32_t)(ax > a.t[2]) << 2) |
-                 ((uint32_t)(ax > a.t[3]) << 3);
-    g &= (1u << NZ) - 1u;
-    rows[i] = RowMeta{xv, float(zone_bias<NZ>(g)) * xv, g, 0u};
-  }
+  // ---- sum the 8 warps' accumulators
   __syncthreads();
-
-  float2 acc[8], gacc[8];
-#pragma unroll
-  for (int p = 0; p < 8; ++p) acc[p] = gacc[p] = make_float2(0.f, 0.f);
-  float bsum = 0.f;
-  float sreg[16];
-
-  const int rb = min(nrows, warp * a.rows_per_warp), re = min(nrows, rb + a.rows_per_warp);
-  const uint32_t* wcol = a.w + jw;
-
-  auto load_row = [&](uint32_t (&P)[4], int i) {
-    const uint32_t m = jvalid ? rows[i].m : 0u;
-    const uint32_t* wr = wcol + (size_t)(k0 + i) * row_words;
-#pragma unroll
-    for (int z = 0; z < 4; ++z) P[z] = (z < NZ && ((m >> z) & 1u)) ? __ldcs(wr + (size_t)z * n16) : 0u;
-  };
-  auto load_scales = [&](int g) {
-#pragma unroll
-    for (int c = 0; c < 16; ++c) sreg[c] = jvalid ? Act<T>::to_f(sc[(size_t)g * a.N + (size_t)c * n16 + jw]) : 0.f;
-  };
-  auto flush = [&]() {
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      acc[p].x = fmaf(sreg[2 * p], fmaf(gacc[p].x, kInvShift, bsum), acc[p].x);
-      acc[p].y = fmaf(sreg[2 * p + 1], fmaf(gacc[p].y, kInvShift, bsum), acc[p].y);
-      gacc[p] = make_float2(0.f, 0.f);
-    }
-    bsum = 0.f;
-  };
-
-  if (rb < re) {
-    int g = (k0 + rb) / a.group;
-    int next_group_k = (g + 1) * a.group;
-    load_scales(g);
-    uint32_t P[D][4];
-#pragma unroll
-    for (int d = 0; d < D; ++d)
-      if (rb + d < re) load_row(P[d], rb + d);
-    for (int r = rb; r < re; r += D) {
-#pragma unroll
-      for (int d = 0; d < D; ++d) {
-        const int i = r + d;
-        if (i < re) {
-          if (k0 + i == next_group_k) {  // K group boundary: apply the finished group's scales
-            flush();
-            next_group_k += a.group;
-            load_scales(++g);
-          }
-          const RowMeta rm = rows[i];
-          bsum += rm.bx;
-          if (rm.m) fma_word(P[d][0], P[d][1], P[d][2], P[d][3], make_float2(rm.x, rm.x), gacc);
-          if (i + D < re) load_row(P[d], i + D);
-        }
-      }
-    }
-    flush();
-  }
-
-  // ---- sum the 8 warps (red aliases the staged rows: wait for every warp first)
-  __syncthreads();
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    red[warp * kTileN + (2 * p) * kTileJ + lane] = acc[p].x;
-    red[warp * kTileN + (2 * p + 1) * kTileJ + lane] = acc[p].y;
-  }
-  __syncthreads();
-  for (int col = threadIdx.x; col < kTileN; col += kThreads) {
+  for (int col = threadIdx.x; col < kSliceN; col += kThreads) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) v += red[w * kTileN + col];
+    for (int w = 0; w < kWarps; ++w) v += red[w * kSliceN + col];
     part[col] = v;
   }
 
@@ -173,10 +225,10 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   cluster.sync();
   const int crank = (int)cluster.block_rank();
   const int csize = (int)cluster.num_blocks();
-  float sum2[kTileN / kThreads];
+  float sum2[kSliceN / kThreads];
   if (crank == 0) {
 #pragma unroll
-    for (int h = 0; h < kTileN / kThreads; ++h) {
+    for (int h = 0; h < kSliceN / kThreads; ++h) {
       const int col = threadIdx.x + h * kThreads;
       float v = 0.f;
       for (int r = 0; r < csize; ++r) v += cluster.map_shared_rank(part, r)[col];
@@ -189,24 +241,24 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
   auto store_y = [&](int col, float v) {
-    const int c = col / kTileJ, jj = col % kTileJ;
-    const int jx = tile * kTileJ + jj;
+    const int c = col / kSliceW, jj = col % kSliceW;
+    const int jx = tile * kSliceW + jj;
     if (jx >= n16) return;
-    const int n = c * n16 + jx;
+    const int nn = c * n16 + jx;
     T out = Act<T>::from_f(v);
-    if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[n]));
-    y[n] = out;
+    if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[nn]));
+    y[nn] = out;
   };
   const int nclu = gridDim.y / csize;
   if (nclu == 1) {
 #pragma unroll
-    for (int h = 0; h < kTileN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
+    for (int h = 0; h < kSliceN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
     return;
   }
   const int clu = split / csize;
 #pragma unroll
-  for (int h = 0; h < kTileN / kThreads; ++h)
-    __stcg(a.slots + ((size_t)tile * nclu + clu) * kTileN + threadIdx.x + h * kThreads, sum2[h]);
+  for (int h = 0; h < kSliceN / kThreads; ++h)
+    __stcg(a.slots + ((size_t)tile * nclu + clu) * kSliceN + threadIdx.x + h * kThreads, sum2[h]);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.counters + tile, 1u) == (unsigned)(nclu - 1);
@@ -214,14 +266,14 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   if (!s_last) return;
   __threadfence();
 #pragma unroll
-  for (int h = 0; h < kTileN / kThreads; ++h) {
+  for (int h = 0; h < kSliceN / kThreads; ++h) {
     const int col = threadIdx.x + h * kThreads;
     float v = 0.f;
     for (int c0 = 0; c0 < nclu; c0 += 8) {
       float buf[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        buf[u] = (c0 + u < nclu) ? __ldcg(a.slots + ((size_t)tile * nclu + c0 + u) * kTileN + col) : 0.f;
+        buf[u] = (c0 + u < nclu) ? __ldcg(a.slots + ((size_t)tile * nclu + c0 + u) * kSliceN + col) : 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u) v += buf[u];
     }
@@ -232,8 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
 
 template <int NZ, typename T>
 int launch_t(const M1Args& a, const M1Plan& p, cudaStream_t st) {
-  constexpr int D = 8;
-  auto kern = m1_kernel<NZ, D, T>;
+  auto kern = m1_kernel<NZ, T>;
   const size_t smem = p.smem_bytes;
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -259,30 +310,34 @@ int launch_t(const M1Args& a, const M1Plan& p, cudaStream_t st) {
 }  // namespace
 
 bool m1_supported(int64_t M, int64_t K, int64_t N, int group) {
-  return M == 1 && N % 16 == 0 && K % group == 0 && group % 8 == 0;
+  // two words per lane: N / 16 even; kD-row blocks never straddle a group
+  return M == 1 && N % 32 == 0 && K % group == 0 && group % kD == 0;
 }
 
 M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
-  constexpr int D = 8;
   M1Plan p{};
   const int64_t n16 = N / 16;
-  p.tiles = (int)((n16 + kTileJ - 1) / kTileJ);
-  const int64_t target = 2LL * (sm_count > 0 ? sm_count : 148);
-  int64_t splits = (target + p.tiles / 2) / p.tiles;
-  const int64_t max_splits = (K + kWarps * D - 1) / (kWarps * D);
+  p.tiles = (int)((n16 + kSliceW - 1) / kSliceW);
+  // one wave: 2 CTAs fit per SM, but 8-CTA clusters pack into the GPCs less densely
+  // (about 1.7 CTAs per SM resident on a 148-SM B200)
+  const int64_t target = (sm_count > 0 ? sm_count : 148) * 17 / 10;
+  int64_t splits = target / p.tiles;
+  const int64_t max_splits = (K + kWarps * kD - 1) / (kWarps * kD);
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
+  p.cluster = (int)(splits < 8 ? splits : 8);
+  splits = splits / p.cluster * p.cluster;
   int64_t rpw = ((K + splits - 1) / splits + kWarps - 1) / kWarps;
-  rpw = (rpw + D - 1) / D * D;
+  rpw = (rpw + kD - 1) / kD * kD;
   p.rows_per_warp = (int)rpw;
   p.rows_per_cta = (int)(rpw * kWarps);
   const int64_t real = (K + p.rows_per_cta - 1) / p.rows_per_cta;
-  p.cluster = (int)(real < 8 ? real : 8);
   p.grid_splits = (int)((real + p.cluster - 1) / p.cluster * p.cluster);
   const int nclu = p.grid_splits / p.cluster;
-  p.slot_bytes = nclu > 1 ? (size_t)p.tiles * nclu * kTileN * sizeof(float) : 0;
+  p.slot_bytes = nclu > 1 ? (size_t)p.tiles * nclu * kSliceN * sizeof(float) : 0;
   p.counter_bytes = nclu > 1 ? (size_t)p.tiles * sizeof(unsigned) : 0;
-  p.smem_bytes = m1_meta_bytes(p.rows_per_cta) + kTileN * sizeof(float);
+  p.smem_bytes = m1_meta_bytes(p.rows_per_cta) + (kWarps + 1) * kSliceN * sizeof(float);
+  (void)group;
   return p;
 }
 

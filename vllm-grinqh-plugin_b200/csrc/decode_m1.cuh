@@ -13,7 +13,7 @@ struct M1Args {
   const void* s;        // [K/group, N] dtype
   const void* bias;     // [N] dtype or null
   void* y;              // [N] dtype
-  float* slots;         // [tiles, clusters per tile, 512] fp32 (several clusters per tile)
+  float* slots;         // [tiles, clusters per tile, 1024] fp32 (several clusters per tile)
   unsigned* counters;   // [tiles] tickets; zero before the first launch, left zero
   int K, N, group, rows_per_warp, rows_per_cta;
   float t[4];
@@ -24,15 +24,16 @@ struct M1Plan {
   size_t slot_bytes, counter_bytes, smem_bytes;
 };
 
-// staged per-row metadata (x, bias*x, grade), 16 bytes a row; aliased by the
-// 8 x 512 fp32 warp-reduction buffer after the main loop
+// staged per-row metadata (x, bias*x, grade), 16 bytes a row
 __host__ __device__ inline size_t m1_meta_bytes(int rows_per_cta) {
-  const size_t meta = (size_t)rows_per_cta * 16;
-  const size_t red = 8 * 512 * 4;
-  return meta > red ? meta : red;
+  return (size_t)rows_per_cta * 16;
 }
 
 bool m1_supported(int64_t M, int64_t K, int64_t N, int group);
+// the kernel reads two packed words (8 bytes) and two scales (4 bytes) at a time
+inline bool m1_pointers_ok(const void* w, const void* s) {
+  return (reinterpret_cast<uintptr_t>(w) % 8) == 0 && (reinterpret_cast<uintptr_t>(s) % 4) == 0;
+}
 M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
 int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st);
 

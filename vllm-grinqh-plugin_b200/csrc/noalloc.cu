@@ -17,10 +17,10 @@ namespace grinqh {
 namespace {
 
 // Fixed scratch shared by every call on a device: tickets first, then the fp32
-// partial sums of the K split. The single-row kernel splits K over at most about
-// 2 CTAs per SM in clusters of 8, so its scratch stays near (2 * SMs / 8) slots of
-// 2 KiB; 256 KiB holds that for every shape on a 148-SM B200. A plan that would
-// need more is rejected rather than overrun.
+// partial sums of the K split. The single-row kernel writes one 4 KiB slot per
+// cluster of up to 8 CTAs (about 1.7 CTAs per SM in one wave), so its scratch stays
+// near (1.7 * SMs / 8) slots, about 128 KiB on a 148-SM B200; 256 KiB holds that
+// for every shape. A plan that would need more is rejected rather than overrun.
 constexpr size_t kNoAllocScratchBytes = size_t(256) << 10;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -68,6 +68,8 @@ extern "C" int grinqh_gemv_noalloc(const void* x, int dtype, int64_t K, const ui
   GRINQH_REQUIRE(K < (1LL << 31) && N < (1LL << 31), "size exceeds int32 range");
   if (!m1_supported(1, K, N, group))
     return set_error(GRINQH_ERR_UNSUPPORTED, "shape K=%lld N=%lld group=%d not supported", (long long)K, (long long)N, group);
+  if (!m1_pointers_ok(w, s))
+    return set_error(GRINQH_ERR_UNSUPPORTED, "weight_packed must be 8-byte and weight_scale 4-byte aligned");
 
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
