@@ -42,6 +42,23 @@ GROUP = 128
 QUANTILES = [0.2, 0.4, 0.6, 0.8]
 
 
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "m1_kernel_gate_up_b8_graded.md")
+
+
+def _committed_traffic(kernel_tag):
+    """DRAM bytes (read + write) of one launch of the dominant kernel, from the
+    committed ncu summary of this benchmark's own launch (a line
+    `traffic_bytes_per_launch: <bytes>` next to `kernel_tag: <tag>`), else None."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            kv = dict(l.strip().split(": ", 1) for l in f if l.startswith(("traffic_bytes_per_launch:", "kernel_tag:")))
+        if kv.get("kernel_tag") == kernel_tag:
+            return int(kv["traffic_bytes_per_launch"])
+    except Exception:
+        pass
+    return None
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -300,6 +317,8 @@ def run_ours(args, rank, world, dev):
         e2e_ms = float(t.item())
     e2e_value = step_bytes * world / (e2e_ms / 1e3) / 1e9
 
+    sweep = None if args.no_sweep else m_sweep(layers, bits, dev, stream)
+
     line = {
         "metric": "quant-linear HBM GB/s, Llama-3-8B layer linears (qkv+o+gate_up+down), decode",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -318,14 +337,56 @@ def run_ours(args, rank, world, dev):
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
                      "bytes_per_launch": per[name], "avg_launch_us": round(kern_ms * 1e3, 3),
-                     "traffic": None},
+                     "traffic": _committed_traffic(f"m1_kernel gate_up b{bits} M{M} graded" if graded else None),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the bench's own gate_up "
+                                       "launch, profiles/m1_kernel_gate_up_b8_graded.md"},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(t_host0, t_host1),
         "per_linear_bytes": per,
     }
+    if sweep is not None:
+        line["m_sweep"] = sweep
     return line
+
+
+def m_sweep(layers, bits, dev, stream, Ms=(16, 128, 1024, 8192)):
+    """configs[1] sweep: each linear at M rows (dense path, as the reference runs rows
+    > 1), two weight copies rotated; per (linear, M): us per call, weight-side bytes/s
+    (packed planes + scales + x + y) and TFLOP/s (2 M N K)."""
+    from grinqh.kernel import grinqh_gemm_or_gemv
+    g = torch.Generator(device=dev).manual_seed(11)
+    out = {}
+    for M in Ms:
+        row = {}
+        for name, (K, N) in SHAPES.items():
+            x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+            R = 8 if M <= 1024 else 2
+            with torch.cuda.stream(stream):
+                for i in range(2):
+                    w, s_ = layers[i % 2][name]
+                    grinqh_gemm_or_gemv(x, w, s_, None, bits, GROUP, N // 4, [0.0] * 4)
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for i in range(R):
+                        w, s_ = layers[i % 2][name]
+                        grinqh_gemm_or_gemv(x, w, s_, None, bits, GROUP, N // 4, [0.0] * 4)
+                gr.replay()
+                torch.cuda.synchronize(dev)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                gr.replay()
+                gr.replay()
+                b.record(stream)
+            torch.cuda.synchronize(dev)
+            us = a.elapsed_time(b) * 1e3 / (2 * R)
+            nbytes = K * N * bits // 8 + (K // GROUP) * N * 2 + 2 * M * K + 2 * M * N
+            row[name] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                         "TFLOP/s": round(2 * M * N * K / us / 1e6, 1)}
+            del gr, x
+        out[str(M)] = row
+    return out
 
 
 # ----------------------------------------------------------------------------- reference (CPU)
@@ -398,6 +459,7 @@ def main():
     ap.add_argument("--m", type=int, default=1, help="decode batch rows per linear")
     ap.add_argument("--bits", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the M = 16..8192 sweep of configs[1]")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -232,6 +232,21 @@ def test_llama_shapes_graded_m1(K, N, b, m1_kernel):
     assert_parity(f32(y)[0], O.to_f32(O.round_to_dtype(ref, "bf16"), "bf16"))
 
 
+@pytest.mark.parametrize("K,N", [(512, 4128), (384, 4112), (1024, 96), (256, 1056)])
+@pytest.mark.parametrize("b", [8, 6, 2])
+def test_ragged_widths_graded_m1(K, N, b, m1_kernel):
+    """Widths that leave a partial 1024-column slice (N = 4128, 1056), fall back to the
+    generic kernel (N / 16 odd: 4112) or fill less than one slice (96)."""
+    from grinqh.kernel import grinqh_gemm_or_gemv
+    from grinqh.utils import pack_codes
+    rng = np.random.default_rng(K * 7 + N + b)
+    codes, s_store, xs, x32, th = _problem(rng, K, N, b, 1)
+    w = pack_codes(torch.from_numpy(codes).cuda(), b)
+    y = grinqh_gemm_or_gemv(dev_act(xs, "bf16"), w, dev_act(s_store, "bf16"), None, b, 128, N // 4, th)
+    ref = O.graded_gemv(x32[0], codes, O.to_f32(s_store, "bf16"), th, b, 128)
+    assert_parity(f32(y)[0], O.to_f32(O.round_to_dtype(ref, "bf16"), "bf16"))
+
+
 @pytest.mark.parametrize("M", [2, 16, 33])
 @pytest.mark.parametrize("b", [8, 4])
 def test_llama_shape_dense_small_m(M, b):
