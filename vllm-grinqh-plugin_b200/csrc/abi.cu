@@ -8,6 +8,7 @@
 #include "decode_m1.cuh"
 #include "gemm_tc.cuh"
 #include "decode_tc.cuh"
+#include "gemm_skinny.cuh"
 
 namespace grinqh {
 
@@ -100,14 +101,23 @@ static bool use_m1tc(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return (kmode == kModeGraded || kmode == kModeUnion) && m1tc_supported(M, K, N, group);
 }
 
-// Rows from which the dense path runs on the tensor cores (tcgen05 GEMM).
-constexpr int64_t kTcMinRows = 64;
+
+// Dense rows up to this count run the skinny tcgen05 GEMM (weights as operand A).
+constexpr int64_t kSkinnyMaxRows = 64;
 
 // Kernel choice: graded / union rows of one token use the register-streaming
-// single-row kernel; dense rows >= kTcMinRows the tcgen05 GEMM; everything else
-// the generic small-M kernel.
+// single-row kernel; dense rows 2..kSkinnyMaxRows the skinny tcgen05 GEMM; dense
+// rows above that the tcgen05 GEMM; everything else the generic small-M kernel.
 static bool use_m1(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return (kmode == kModeGraded || kmode == kModeUnion) && m1_supported(M, K, N, group);
+}
+
+static bool use_skinny(int kmode, int64_t M, int64_t K, int64_t N, int group) {
+  return kmode == kModeDense && M >= 2 && M <= kSkinnyMaxRows && skinny_supported(M, K, N, group);
+}
+
+static size_t workspace_for(const SkinnyPlan& p) {
+  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
 }
 
 static int validate(const void* x, int dtype, int64_t M, int64_t K, const void* w, const void* s, int bits,
@@ -159,8 +169,14 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
     const size_t b = workspace_for(plan_decode(M, K, N, km, sms));
     return a > b ? a : b;
   }
-  if (km == kModeDense && M >= kTcMinRows && K % 64 == 0 && group_size % 64 == 0) return 0;  // tcgen05 GEMM
-  return workspace_for(plan_decode(M, K, N, km, sms));
+  // an activation or output view that the tensor-core kernels cannot take (alignment)
+  // runs the generic kernel, and this query does not see the pointers: cover both
+  const size_t generic = workspace_for(plan_decode(M, K, N, km, sms));
+  if (use_skinny(km, M, K, N, group_size)) {
+    const size_t a = workspace_for(plan_skinny(M, K, N, sms));
+    return a > generic ? a : generic;
+  }
+  return generic;
 }
 
 extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
@@ -228,7 +244,37 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_m1(g, plan, dtype, max_bits / 2, stream);
   }
 
-  if (km == kModeDense && M >= kTcMinRows && gemm_tc_supported(M, K, N, group, x, y)) {
+  if (use_skinny(km, M, K, N, group) && skinny_pointers_ok(x, y)) {
+    const SkinnyPlan plan = plan_skinny(M, K, N, sms);
+    const size_t need = workspace_for(plan);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
+    SkinnyArgs g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.M = (int)M;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    g.tiles = plan.tiles;
+    g.splits = plan.splits;
+    g.cluster = plan.cluster;
+    g.steps_per_split = plan.steps_per_split;
+    if (need > 0) {
+      char* base = static_cast<char*>(workspace);
+      g.slots = reinterpret_cast<float*>(base);
+      g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
+      const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
+      if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    return launch_skinny(g, plan, dtype, max_bits / 2, stream);
+  }
+
+  if (km == kModeDense && M > kSkinnyMaxRows && gemm_tc_supported(M, K, N, group, x, y)) {
     GemmArgs g{};
     g.x = x;
     g.w = w;
@@ -273,7 +319,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
   GRINQH_RETURN_IF(check_device());
-  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts();
+  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts() + take_skinny_timeouts();
   if (timeouts) *timeouts = v;
   return GRINQH_OK;
 }

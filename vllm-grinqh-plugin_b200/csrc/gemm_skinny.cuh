@@ -1,0 +1,35 @@
+// Host-side interface of the skinny tcgen05 GEMM (gemm_skinny.cu): dense rows
+// 2..64 with the weights as the MMA's A operand and the tokens as its N.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace grinqh {
+
+struct SkinnyArgs {
+  const void* x;        // [M, K] dtype, row-major, 16-byte aligned
+  const uint32_t* w;    // [K, nz*N/16] packed planes
+  const void* s;        // [K/group, N] dtype
+  const void* bias;     // [N] dtype or null
+  void* y;              // [M, N] dtype
+  float* slots;         // [tiles, clusters, Mp * 512] fp32 cluster sums (several clusters per tile)
+  unsigned* counters;   // [tiles, cluster size] tickets; zero before the first launch, left zero
+  int M, K, N, group;
+  int tiles, splits, cluster, steps_per_split;
+};
+
+struct SkinnyPlan {
+  int mp;                // tokens rounded up to 16 (the MMA's N)
+  int tiles, splits, cluster, steps_per_split;
+  size_t slot_bytes, counter_bytes;
+};
+
+bool skinny_supported(int64_t M, int64_t K, int64_t N, int group);
+bool skinny_pointers_ok(const void* x, const void* y);
+SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count);
+int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st);
+unsigned take_skinny_timeouts();
+
+}  // namespace grinqh
