@@ -244,7 +244,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_m1(g, plan, dtype, max_bits / 2, stream);
   }
 
-  if (use_skinny(km, M, K, N, group) && skinny_pointers_ok(x, y)) {
+  if (use_skinny(km, M, K, N, group) && skinny_pointers_ok(x, w, s)) {
     const SkinnyPlan plan = plan_skinny(M, K, N, sms);
     const size_t need = workspace_for(plan);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))

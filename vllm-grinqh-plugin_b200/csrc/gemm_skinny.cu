@@ -5,19 +5,22 @@
 // are operand B (N = the row count rounded up to 16).
 //
 // A CTA owns a tile of 32 packed words (512 output columns) and a range of K steps
-// of 64 rows:
-//   warps 0-15  converters: load the planes of 64 rows x 32 words (two steps ahead),
-//               merge them into codes, multiply by the group scale, round to the
-//               activation dtype -- the reference's dtype(w * s), bit for bit -- and
-//               store the 512 x 64 tile MN-major with the 128-byte swizzle (a lane's
-//               16 columns of one row are 32 contiguous bytes). After the K loop they
-//               are the epilogue.
-//   warp 16     TMA producer: the Mp x 64 activation tile (rows past M read as 0),
-//               K-major, 128-byte swizzle.
-//   warp 17     allocates TMEM and issues, per 16-deep K slice, four
-//               tcgen05.mma kind::f16 (one per 128-column block, N = Mp) from one
-//               thread; tcgen05.commit frees the stage.
-// Three stages (64 KB of weights + up to 8 KB of activations each) are in flight.
+// of 32 rows. Three rings of shared-memory stages:
+//   planes  (5 x 16 KB)  the b/2 plane words of 32 rows x 32 words, one 2-D TMA box
+//                        per plane (128-byte swizzle), loaded up to five steps ahead
+//                        by warp 16;
+//   weights (4 x 32 KB)  operand A: dtype(w * s) for 512 columns x 32 rows, MN-major
+//                        with the 128-byte swizzle;
+//   x       (4 x 4 KB)   operand B: Mp x 32 activations, K-major with the 64-byte
+//                        swizzle (rows past M read as 0), loaded by TMA.
+// Warps 0-15 convert (a warp covers 8 rows x 4 word pairs, so that every shared-memory
+// access is free of bank conflicts): each thread owns two neighbouring words of one row, reads their
+// planes from shared memory, merges them into codes, multiplies by the group scale,
+// rounds once to the activation dtype -- the reference's dtype(w * s), bit for bit --
+// and stores the weight stage; thread 0 also loads each step's x tile. Warp 17 issues
+// the MMAs (per 16-deep K slice, one tcgen05.mma kind::f16 per 128-column block,
+// N = Mp) from one thread into TMEM; tcgen05.commit frees the stage. The converters
+// never wait on global memory: the plane ring hides its latency.
 //
 // K is split over the CTAs of a thread-block cluster (and over several clusters for
 // long K). Each CTA stages its fp32 partial tile in shared memory; rank r of the
@@ -40,19 +43,27 @@ namespace {
 
 constexpr int TW = 32;         // packed words per tile
 constexpr int TN = 16 * TW;    // output columns per tile
-constexpr int BK = 64, STAGES = 3;
+constexpr int BK = 32;         // rows per K step
+constexpr int SP = 5, SW = 4;  // plane stages; weight / activation stages
 constexpr int kConvWarps = 16;
-constexpr int kProdWarp = 16, kMmaWarp = 17;
+constexpr int kLoadWarp = 16, kMmaWarp = 17;
 constexpr int kThreads = 32 * (kConvWarps + 2);
 constexpr int kMaxMp = 64;
-constexpr uint32_t kStageW = TN * BK * 2;      // 64 KB
-constexpr uint32_t kStageX = kMaxMp * BK * 2;  // 8 KB
-constexpr uint32_t kSmemBytes = STAGES * (kStageW + kStageX) + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t kLbo = 8 * 1024;  // weights: stride between 64-column MN atoms (8 K atoms of 1 KB)
-constexpr uint32_t kSbo = 1024;      // stride between 8-row K groups
+constexpr uint32_t kPlaneBytes = BK * TW * 4;  // one plane of a step: 4 KB
+constexpr uint32_t kStageP = 4 * kPlaneBytes;  // 16 KB
+constexpr uint32_t kStageW = TN * BK * 2;      // 32 KB
+constexpr uint32_t kStageX = kMaxMp * BK * 2;  // 4 KB
+constexpr uint32_t kOffW = SP * kStageP;
+constexpr uint32_t kOffX = kOffW + SW * kStageW;
+constexpr uint32_t kOffBar = kOffX + SW * kStageX;
+constexpr uint32_t kSmemBytes = kOffBar + 256 /*barriers*/ + 1024 /*align*/;
+constexpr uint32_t kLbo = 4 * 1024;  // weights: stride between 64-column MN atoms (4 K atoms of 1 KB)
+constexpr uint32_t kSbo = 1024;      // weights: stride between 8-row K groups
+constexpr uint32_t kSboX = 512;      // x: stride between 8-row groups of 64-byte rows
 constexpr int kPartRow = 16 * 33;    // fp32 partial staging [m][c][word], words padded to 33
 
-static_assert((size_t)kMaxMp * kPartRow * 4 <= (size_t)STAGES * (kStageW + kStageX), "partial tile must fit");
+static_assert((size_t)kMaxMp * kPartRow * 4 <= kOffBar, "partial tile must fit in the stages");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 
 template <typename T> struct Fmt;
 template <> struct Fmt<__nv_bfloat16> {
@@ -61,6 +72,9 @@ template <> struct Fmt<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ float2 unpack(uint32_t bits) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bits));
+  }
 };
 template <> struct Fmt<__half> {
   static constexpr uint32_t v = 0;
@@ -68,32 +82,33 @@ template <> struct Fmt<__half> {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ float2 unpack(uint32_t bits) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&bits));
+  }
 };
 
-// byte offset of the 16-byte chunk `chunk16` (8 columns) of row k in a weight stage
-// (MN-major, 128-byte swizzle)
-__device__ __forceinline__ uint32_t w_off(int chunk16, int k) {
-  const int atom_mn = chunk16 >> 3, c = chunk16 & 7;
-  const int atom_k = k >> 3, r = k & 7;
-  return (uint32_t)(atom_mn * kLbo + atom_k * kSbo + r * 128 + ((c ^ r) << 4));
+__device__ __forceinline__ uint64_t* bar_at(unsigned char* smem, int i) {
+  return reinterpret_cast<uint64_t*>(smem + kOffBar) + i;
 }
 
 template <int NZ, typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    skinny_kernel(const __grid_constant__ CUtensorMap tmap_x, const SkinnyArgs a, const int mp) {
+    skinny_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                  const SkinnyArgs a, const int mp) {
   constexpr int kShift = 8 - 2 * NZ;
-  constexpr float kInvShift = 1.0f / float(1 << kShift);
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sW = smem;
-  unsigned char* sX = smem + STAGES * kStageW;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * (kStageW + kStageX));
-  uint64_t* x_full = bars;
-  uint64_t* w_full = bars + STAGES;
-  uint64_t* empty = bars + 2 * STAGES;
-  uint64_t* acc_full = bars + 3 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+  unsigned char* sP = smem;
+  unsigned char* sW = smem + kOffW;
+  unsigned char* sX = smem + kOffX;
+  uint64_t* p_full = bar_at(smem, 0);
+  uint64_t* p_empty = bar_at(smem, SP);
+  uint64_t* x_full = bar_at(smem, 2 * SP);
+  uint64_t* w_full = bar_at(smem, 2 * SP + SW);
+  uint64_t* empty = bar_at(smem, 2 * SP + 2 * SW);
+  uint64_t* acc_full = bar_at(smem, 2 * SP + 3 * SW);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_at(smem, 2 * SP + 3 * SW + 1));
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,7 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tcols = 4 * cstride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < SP; ++s) {
+      mbar_init(&p_full[s], 1);
+      mbar_init(&p_empty[s], kConvWarps);
+    }
+    for (int s = 0; s < SW; ++s) {
       mbar_init(&x_full[s], 1);
       mbar_init(&w_full[s], kConvWarps);
       mbar_init(&empty[s], 1);
@@ -121,16 +140,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kProdWarp) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ plane loader
     if (lane == 0) {
-      prefetch_tmap(&tmap_x);
-      const uint32_t xbytes = (uint32_t)mp * BK * 2;
+      prefetch_tmap(&tmap_w);
       for (int i = 0; i < nq; ++i) {
-        const int s = i % STAGES;
-        if (i >= STAGES) mbar_wait(&empty[s], ((i / STAGES) - 1) & 1);
-        mbar_arrive_expect_tx(&x_full[s], xbytes);
-        tma_load_2d(sX + s * kStageX, &tmap_x, (q0 + i) * BK, 0, &x_full[s]);
+        const int s = i % SP;
+        if (i >= SP) mbar_wait(&p_empty[s], ((i / SP) - 1) & 1);
+        mbar_arrive_expect_tx(&p_full[s], NZ * kPlaneBytes);
+        const int row = (q0 + i) * BK;
+#pragma unroll
+        for (int z = 0; z < NZ; ++z)
+          tma_load_2d(sP + s * kStageP + z * kPlaneBytes, &tmap_w, z * n16 + jt0, row, &p_full[s]);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -138,8 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = instr_desc(1, Fmt<T>::v, Fmt<T>::v, 1, 0, (uint32_t)mp, 128);
       for (int i = 0; i < nq; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
+        const int s = i % SW;
+        const uint32_t ph = (i / SW) & 1;
         mbar_wait(&x_full[s], ph);
         mbar_wait(&w_full[s], ph);
         tc_fence_after();
@@ -147,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t xbase = smem_u32(sX + s * kStageX);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t bdesc = smem_desc(xbase + kk * 32, 16, 1024, 2);
+          const uint64_t bdesc = smem_desc(xbase + kk * 32, 16, kSboX, 4);
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const uint64_t adesc = smem_desc(wbase + b * 2 * kLbo + kk * 2 * kSbo, kLbo, kSbo, 2);
@@ -160,79 +181,115 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ converters
-    const int ct = threadIdx.x;      // 0..511
-    const int jj = ct & (TW - 1);    // word of the tile this thread converts
-    const int r0 = ct / TW;          // rows r0 + 16 i, i = 0..3
-    const int jw = jt0 + jj;
-    const bool jvalid = jw < n16;
-    const size_t row_words = (size_t)NZ * n16;
-    const uint32_t* wcol = a.w + (jvalid ? jw : 0);
-    const T* sc = static_cast<const T*>(a.s);
-    const int spg = a.group / BK;  // K steps per scale group
-    float sreg[16], snext[16];
-    auto load_scales = [&](float (&dst)[16], int g) {
+    // a warp covers 8 rows x 4 word pairs: in every shared-memory access the 8 lanes of
+    // a phase are 8 different rows, which the 128-byte swizzle spreads over all banks
+    const int ct = threadIdx.x;                      // 0..511
+    const int rr = 8 * (warp & 3) + (lane & 7);      // row rr of each step
+    const int jp = 4 * (warp >> 2) + (lane >> 3);    // this thread's words: 2 jp, 2 jp + 1
+    const int jw = jt0 + 2 * jp;
+    const bool jvalid = jw < n16;      // n16 is even: both words are valid or neither
+    const int spg = a.group / BK;      // K steps per scale group
+    const bool x_issuer = ct == 0;
+    if (x_issuer) prefetch_tmap(&tmap_x);
+    const uint32_t xbytes = (uint32_t)mp * BK * 2;
+    // scales of column group c for the two words, s[g, c * n16 + jw .. jw + 1] (the
+    // 2^-shift of the shifted codes is in the magic constant below); the next group's
+    // are prefetched as packed dtype pairs
+    float2 sreg[16];
+    uint32_t snext[16];
+    auto load_scales = [&](int g) {
+      const uint32_t* sp =
+          reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.s) + (size_t)g * a.N + (jvalid ? jw : 0));
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        dst[c] = jvalid ? Act<T>::to_f(sc[(size_t)g * a.N + (size_t)c * n16 + jw]) * kInvShift : 0.f;
+      for (int c = 0; c < 16; ++c) snext[c] = jvalid ? __ldg(sp + (size_t)c * (n16 >> 1)) : 0u;
     };
-    uint32_t P1[4][4], P2[4][4];
-    auto load_planes = [&](uint32_t (&P)[4][4], int i) {
-      const int q = q0 + i;
+    auto unpack_scales = [&]() {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const uint32_t* wr = wcol + (size_t)(q * BK + r0 + 16 * r) * row_words;
-#pragma unroll
-        for (int z = 0; z < 4; ++z) P[r][z] = (z < NZ && jvalid && i < nq) ? __ldcs(wr + (size_t)z * n16) : 0u;
+      for (int c = 0; c < 16; ++c) {
+        sreg[c] = Fmt<T>::unpack(snext[c]);
       }
     };
     if (nq > 0) {
       const int g0 = q0 / spg;
-      load_scales(sreg, g0);
-      if ((g0 + 1) * spg < q0 + nq) load_scales(snext, g0 + 1);
+      load_scales(g0);
+      unpack_scales();
+      if ((g0 + 1) * spg < q0 + nq) load_scales(g0 + 1);
     }
-    auto convert_step = [&](const uint32_t (&Pc)[4][4], int i) {
-      const int q = q0 + i, s = i % STAGES;
+    // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
+    // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u
+    constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
+    constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
+    // store offsets of row rr in the weight stage (MN-major, 128-byte swizzle: 16-byte
+    // chunk c of row k sits at (c ^ (k & 7)))
+    const uint32_t rsw = (uint32_t)(rr & 7);
+    const uint32_t c0 = (uint32_t)(4 * jp) & 7u;  // first of the thread's four chunks (0 or 4)
+    const uint32_t row_base = (uint32_t)(((4 * jp) >> 3) * kLbo + (rr >> 3) * kSbo + (rr & 7) * 128);
+    uint32_t chunk_off[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) chunk_off[e] = ((c0 + (uint32_t)e) ^ rsw) << 4;
+
+    for (int i = 0; i < nq; ++i) {
+      const int q = q0 + i, s = i % SW, ps = i % SP;
       if (i > 0 && q % spg == 0) {  // next scale group: its scales were prefetched
+        unpack_scales();
         const int g = q / spg;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) sreg[c] = snext[c];
-        if ((g + 1) * spg < q0 + nq) load_scales(snext, g + 1);
+        if ((g + 1) * spg < q0 + nq) load_scales(g + 1);
       }
-      if (i >= STAGES) mbar_wait(&empty[s], ((i / STAGES) - 1) & 1);
-      unsigned char* wst = sW + s * kStageW;
+      if (i >= SW) mbar_wait(&empty[s], ((i / SW) - 1) & 1);
+      if (x_issuer) {
+        mbar_arrive_expect_tx(&x_full[s], xbytes);
+        tma_load_2d(sX + s * kStageX, &tmap_x, q * BK, 0, &x_full[s]);
+      }
+      mbar_wait(&p_full[ps], (i / SP) & 1);
+      // plane words of the two words of row rr (the planes are 128-byte swizzled by the
+      // TMA: 16-byte chunk c of row r sits at chunk c ^ (r & 7))
+      uint2 P[4];
+      const unsigned char* pst =
+          sP + ps * kStageP + rr * (TW * 4) + ((((uint32_t)jp >> 1) ^ (uint32_t)(rr & 7)) << 4) + (jp & 1) * 8;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        uint32_t qv[4];
-        merge_planes(Pc[r][0] ^ kSignFlip, Pc[r][1], Pc[r][2], Pc[r][3], qv);
-        uint32_t out[8];
+      for (int z = 0; z < 4; ++z)
+        P[z] = z < NZ ? *reinterpret_cast<const uint2*>(pst + z * kPlaneBytes) : make_uint2(0u, 0u);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_empty[ps]);
+
+      unsigned char* wst = sW + s * kStageW;
+      {
+        uint32_t qa[4], qb[4];  // merged code bytes of word 2 jp (a) and 2 jp + 1 (b)
+        merge_planes(P[0].x ^ kSignFlip, P[1].x, P[2].x, P[3].x, qa);
+        merge_planes(P[0].y ^ kSignFlip, P[1].y, P[2].y, P[3].y, qb);
+        uint32_t oa[8], ob[8];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
+          float2 v[4];  // column 4t + L of (word a, word b) times its scale
+#pragma unroll
+          for (int L = 0; L < 4; ++L) {
+            const uint32_t sel = 0x7440u | (uint32_t)L;
+            const float2 f = make_float2(__int_as_float(__byte_perm(qa[t], kMagicBits, sel)),
+                                         __int_as_float(__byte_perm(qb[t], kMagicBits, sel)));
+            const float2 sc = sreg[4 * t + L];
+            if constexpr (Fmt<T>::v == 1) {
+              // bf16 scale (8 significant bits): (2^23 + 128) * s / 2^shift is exact in
+              // fp32, so one fused multiply-add gives code * s exactly
+              v[L] = __ffma2_rn(f, sc, make_float2(-kMagic * sc.x, -kMagic * sc.y));
+            } else {
+              v[L] = __fmul2_rn(__fadd2_rn(f, make_float2(-kMagic, -kMagic)), sc);
+            }
+          }
           // code * s exactly in fp32, rounded once to the activation dtype (kernel.py:586)
-          const float f0 = byte_to_float<0>(qv[t]) * sreg[4 * t + 0];
-          const float f1 = byte_to_float<1>(qv[t]) * sreg[4 * t + 1];
-          const float f2 = byte_to_float<2>(qv[t]) * sreg[4 * t + 2];
-          const float f3 = byte_to_float<3>(qv[t]) * sreg[4 * t + 3];
-          out[2 * t] = Fmt<T>::pack(f0, f1);
-          out[2 * t + 1] = Fmt<T>::pack(f2, f3);
+          oa[2 * t] = Fmt<T>::pack(v[0].x, v[1].x);
+          oa[2 * t + 1] = Fmt<T>::pack(v[2].x, v[3].x);
+          ob[2 * t] = Fmt<T>::pack(v[0].y, v[1].y);
+          ob[2 * t + 1] = Fmt<T>::pack(v[2].y, v[3].y);
         }
-        const int k = r0 + 16 * r;
-        *reinterpret_cast<uint4*>(wst + w_off(2 * jj, k)) = make_uint4(out[0], out[1], out[2], out[3]);
-        *reinterpret_cast<uint4*>(wst + w_off(2 * jj + 1, k)) = make_uint4(out[4], out[5], out[6], out[7]);
+        unsigned char* rowp = wst + row_base;
+        *reinterpret_cast<uint4*>(rowp + chunk_off[0]) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+        *reinterpret_cast<uint4*>(rowp + chunk_off[1]) = make_uint4(oa[4], oa[5], oa[6], oa[7]);
+        *reinterpret_cast<uint4*>(rowp + chunk_off[2]) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+        *reinterpret_cast<uint4*>(rowp + chunk_off[3]) = make_uint4(ob[4], ob[5], ob[6], ob[7]);
       }
       fence_proxy_async_smem();  // make the generic-proxy stores visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_full[s]);
-    };
-    // the plane buffers rotate by name: a register copy of a pending load would wait for it
-    load_planes(P1, 0);
-    load_planes(P2, 1);
-    for (int i = 0; i < nq; i += 2) {
-      convert_step(P1, i);
-      load_planes(P1, i + 2);
-      if (i + 1 < nq) {
-        convert_step(P2, i + 1);
-        load_planes(P2, i + 3);
-      }
     }
 
     // ------------------------------------------------------------ partial tile -> smem
@@ -242,21 +299,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(acc_full, 0);
     tc_fence_after();
     float* part = reinterpret_cast<float*>(smem);  // the stages are idle now
-    const int quarter = warp & 3, blk = warp >> 2;
-    const int pos = blk * 128 + quarter * 32 + lane;
-    const int pw = pos >> 4, pc = pos & 15;
-    for (int h = 0; h < (int)cstride; h += 32) {
-      uint32_t r[32];
-      if (nq > 0) {
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + blk * cstride + h, r);
-        tmem_ld_wait();
-      } else {
+    const int quarter = warp & 3;
+    {
+      const int blk = warp >> 2;
+      const int pos = blk * 128 + quarter * 32 + lane;
+      const int pw = pos >> 4, pc = pos & 15;
+      for (int h = 0; h < (int)cstride; h += 32) {
+        uint32_t r[32];
+        if (nq > 0) {
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + blk * cstride + h, r);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) r[t] = 0u;
+          for (int t = 0; t < 32; ++t) r[t] = 0u;
+        }
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          if (h + t < mp) part[(h + t) * kPartRow + pc * 33 + pw] = __uint_as_float(r[t]);
       }
-#pragma unroll
-      for (int t = 0; t < 32; ++t)
-        if (h + t < mp) part[(h + t) * kPartRow + pc * 33 + pw] = __uint_as_float(r[t]);
     }
   }
   tc_fence_before();
@@ -267,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
   const float* part = reinterpret_cast<const float*>(smem);
-  // (row m, column group c, word jj) -> y[m, c * n16 + jt0 + jj]; one warp writes a
+  // (row m, column group c, word w) -> y[m, c * n16 + jt0 + w]; one warp writes a
   // pair's 32 words (64 contiguous bytes)
   auto store_y = [&](int m, int c, int w, float v) {
     if (m >= a.M || jt0 + w >= n16) return;
@@ -294,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pr = crank + cs * k;
     const int off = (pr >> 4) * kPartRow + (pr & 15) * 33 + lane;
     float v = 0.f;
-    for (int rr = 0; rr < cs; ++rr) v += cluster.map_shared_rank(part, rr)[off];
+    for (int r = 0; r < cs; ++r) v += cluster.map_shared_rank(part, r)[off];
     if (nclu == 1) store_y(pr >> 4, pr & 15, lane, v);
     else __stcg(myslot + (size_t)pr * 32 + lane, v);
   }
@@ -337,16 +397,31 @@ template <int NZ, typename T>
 int launch_t(const SkinnyArgs& a, const SkinnyPlan& p, cudaStream_t st) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  CUtensorMap tmap;
-  const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-  const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
-  const cuuint32_t box[2] = {BK, (cuuint32_t)p.mp};
   const cuuint32_t estride[2] = {1, 1};
-  const CUresult r = enc(&tmap, Fmt<T>::v ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                         const_cast<void*>(a.x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  // activations [M, K]: boxes of 32 K-elements (64 bytes) x Mp rows, 64-byte swizzle
+  CUtensorMap tmap_x;
+  {
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+    const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)p.mp};
+    const CUresult r = enc(&tmap_x, Fmt<T>::v ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           2, const_cast<void*>(a.x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed (%d)", (int)r);
+  }
+  // packed planes [K, nz * N/16] uint32: boxes of 32 words (128 bytes) x 32 rows,
+  // 128-byte swizzle (conflict-free reads by the converters)
+  CUtensorMap tmap_w;
+  {
+    const cuuint64_t gdim[2] = {(cuuint64_t)NZ * (a.N / 16), (cuuint64_t)a.K};
+    const cuuint64_t gstride[1] = {(cuuint64_t)NZ * (a.N / 16) * 4};
+    const cuuint32_t box[2] = {TW, BK};
+    const CUresult r = enc(&tmap_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(a.w), gdim, gstride,
+                           box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed (%d)", (int)r);
+  }
   auto kern = skinny_kernel<NZ, T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -362,7 +437,7 @@ int launch_t(const SkinnyArgs& a, const SkinnyPlan& p, cudaStream_t st) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, tmap, a, p.mp);
+  e = cudaLaunchKernelEx(&cfg, kern, tmap_x, tmap_w, a, p.mp);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "skinny GEMM launch: %s", cudaGetErrorString(e));
   return check_launch("skinny GEMM");
 }
@@ -377,13 +452,15 @@ unsigned take_skinny_timeouts() {
 }
 
 bool skinny_supported(int64_t M, int64_t K, int64_t N, int group) {
-  // TMA rows of 64 K-elements, K steps that never straddle a scale group, N / 16 words
-  return M >= 2 && M <= kMaxMp && K % BK == 0 && group % BK == 0 && N % 16 == 0 && K < (1LL << 31);
+  // K steps of 32 rows that never straddle a scale group; plane boxes start on 16-byte
+  // boundaries (N / 16 words per plane a multiple of 4, so N % 64 == 0); a thread's two
+  // words and their two scales are one 8-byte and one 4-byte load
+  return M >= 2 && M <= kMaxMp && K % BK == 0 && group % BK == 0 && N % 64 == 0 && K < (1LL << 31);
 }
 
-bool skinny_pointers_ok(const void* x, const void* y) {
-  (void)y;
-  return (reinterpret_cast<uintptr_t>(x) % 16) == 0;
+bool skinny_pointers_ok(const void* x, const void* w, const void* s) {
+  return (reinterpret_cast<uintptr_t>(x) % 16) == 0 && (reinterpret_cast<uintptr_t>(w) % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(s) % 4) == 0;
 }
 
 SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
@@ -392,7 +469,7 @@ SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
   const int64_t n16 = N / 16;
   p.tiles = (int)((n16 + TW - 1) / TW);
   const int64_t nk = K / BK;
-  // one CTA per SM (about 218 KB of shared memory each); clusters of up to 8 pack
+  // one CTA per SM (about 200 KB of shared memory each); clusters of up to 8 pack
   // into the GPCs less densely than single CTAs, so aim a little under the SM count
   const int64_t target = (sm_count > 0 ? sm_count : 148) * 7 / 8;
   int64_t splits = target / p.tiles;

@@ -27,7 +27,7 @@ struct SkinnyPlan {
 };
 
 bool skinny_supported(int64_t M, int64_t K, int64_t N, int group);
-bool skinny_pointers_ok(const void* x, const void* y);
+bool skinny_pointers_ok(const void* x, const void* w, const void* s);
 SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count);
 int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st);
 unsigned take_skinny_timeouts();

@@ -42,15 +42,26 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// One try_wait; the thread is suspended in hardware (up to the hint, in ns) until the
-// phase completes instead of spinning on issue slots.
+// One try_wait; the thread may be suspended in hardware (up to the hint, in ns) until
+// the phase completes instead of spinning on issue slots.
+#ifndef GRINQH_WAIT_HINT_NS
+#define GRINQH_WAIT_HINT_NS 1000000u
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#if GRINQH_WAIT_HINT_NS == 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_u32(bar)), "r"(parity), "r"((uint32_t)GRINQH_WAIT_HINT_NS)
       : "memory");
+#endif
   return ok != 0;
 }
 
