@@ -78,18 +78,43 @@ static int resolve_mode(int mode, int64_t M) {
   }
 }
 
+// Workspace layout of every split-K kernel: the tickets first, in a region of at
+// least kTicketBytes, then the fp32 partial sums. The kernels return every ticket to
+// zero and nothing else is ever written into the ticket region, so a workspace reused
+// by calls of any shape keeps that region zero (GRINQH_WORKSPACE_ZEROED).
+constexpr size_t kTicketBytes = 16 << 10;
+
+static size_t ticket_region(size_t counter_bytes) {
+  return counter_bytes > kTicketBytes ? align_up(counter_bytes, 256) : kTicketBytes;
+}
+
+static size_t split_workspace(size_t partial_bytes, size_t counter_bytes) {
+  if (counter_bytes == 0) return 0;
+  return ticket_region(counter_bytes) + align_up(partial_bytes, 256);
+}
+
+// Points tickets and partial sums into the workspace; clears the tickets unless the
+// caller says they are zero (and they fit the region that is kept zero).
+static int bind_workspace(void* workspace, size_t partial_bytes, size_t counter_bytes, bool zeroed,
+                          cudaStream_t stream, float** partial, unsigned** counters) {
+  char* base = static_cast<char*>(workspace);
+  *counters = reinterpret_cast<unsigned*>(base);
+  *partial = reinterpret_cast<float*>(base + ticket_region(counter_bytes));
+  if (!zeroed || counter_bytes > kTicketBytes) {
+    const cudaError_t e = cudaMemsetAsync(*counters, 0, counter_bytes, stream);
+    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
+  return GRINQH_OK;
+}
+
 static size_t workspace_for(const DecodePlan& p) {
   if (p.ksplit <= 1) return 0;
-  return align_up(p.partial_bytes, 256) + align_up(p.counter_bytes, 256);
+  return split_workspace(p.partial_bytes, p.counter_bytes);
 }
 
-static size_t workspace_for(const M1Plan& p) {
-  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
-}
+static size_t workspace_for(const M1Plan& p) { return split_workspace(p.slot_bytes, p.counter_bytes); }
 
-static size_t workspace_for(const M1TcPlan& p) {
-  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
-}
+static size_t workspace_for(const M1TcPlan& p) { return split_workspace(p.slot_bytes, p.counter_bytes); }
 
 // The int8 tensor-core single-row kernel (decode_tc.cu) is selected only when
 // GRINQH_M1_TENSOR_CORES=1: it is exact but slower than the register-streaming
@@ -116,9 +141,7 @@ static bool use_skinny(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return kmode == kModeDense && M >= 2 && M <= kSkinnyMaxRows && skinny_supported(M, K, N, group);
 }
 
-static size_t workspace_for(const SkinnyPlan& p) {
-  return align_up(p.slot_bytes, 256) + align_up(p.counter_bytes, 256);
-}
+static size_t workspace_for(const SkinnyPlan& p) { return split_workspace(p.slot_bytes, p.counter_bytes); }
 
 static int validate(const void* x, int dtype, int64_t M, int64_t K, const void* w, const void* s, int bits,
                     int group, int64_t N, const void* y) {
@@ -156,6 +179,7 @@ extern "C" const char* grinqh_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int group_size, int mode) {
   if (group_size <= 0 || !valid_bits(max_bits)) return 0;
+  mode &= ~GRINQH_WORKSPACE_ZEROED;
   const int km = resolve_mode(mode, M);
   if (km < 0 || M <= 0 || K <= 0 || N <= 0) return 0;
   int sms = 148;
@@ -186,6 +210,8 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   int dev = 0, sms = 0;
   GRINQH_RETURN_IF(device_info(&dev, &sms));
   GRINQH_RETURN_IF(validate(x, dtype, M, K, w, s, max_bits, group, N, y));
+  const bool zeroed = (mode & GRINQH_WORKSPACE_ZEROED) != 0;  // tickets already zero: no clearing
+  mode &= ~GRINQH_WORKSPACE_ZEROED;
   const int km = resolve_mode(mode, M);
   GRINQH_REQUIRE(km >= 0, "unknown mode %d", mode);
   GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
@@ -208,11 +234,8 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     g.tiles = plan.tiles;
     g.units_per_cta = plan.units_per_cta;
     for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
-    char* base = static_cast<char*>(workspace);
-    g.slots = reinterpret_cast<float*>(base);
-    g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
-    const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
-    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
+                                    &g.counters));
     return launch_m1tc(g, plan, dtype, max_bits / 2, stream);
   }
 
@@ -234,13 +257,9 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     g.rows_per_warp = plan.rows_per_warp;
     g.rows_per_cta = plan.rows_per_cta;
     for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
-    if (need > 0) {
-      char* base = static_cast<char*>(workspace);
-      g.slots = reinterpret_cast<float*>(base);
-      g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
-      const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
-      if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    }
+    if (need > 0)
+      GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
+                                      &g.counters));
     return launch_m1(g, plan, dtype, max_bits / 2, stream);
   }
 
@@ -264,13 +283,9 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     g.splits = plan.splits;
     g.cluster = plan.cluster;
     g.steps_per_split = plan.steps_per_split;
-    if (need > 0) {
-      char* base = static_cast<char*>(workspace);
-      g.slots = reinterpret_cast<float*>(base);
-      g.counters = reinterpret_cast<unsigned*>(base + align_up(plan.slot_bytes, 256));
-      const cudaError_t e = cudaMemsetAsync(g.counters, 0, plan.counter_bytes, stream);
-      if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    }
+    if (need > 0)
+      GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
+                                      &g.counters));
     return launch_skinny(g, plan, dtype, max_bits / 2, stream);
   }
 
@@ -307,13 +322,9 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   a.rows_per_cta = plan.rows_per_cta;
   a.ksplit = plan.ksplit;
   for (int z = 0; z < 4; ++z) a.t[z] = thresholds ? thresholds[z] : 0.0f;
-  if (plan.ksplit > 1) {
-    char* base = static_cast<char*>(workspace);
-    a.partial = reinterpret_cast<float*>(base);
-    a.counters = reinterpret_cast<unsigned*>(base + align_up(plan.partial_bytes, 256));
-    const cudaError_t e = cudaMemsetAsync(a.counters, 0, plan.counter_bytes, stream);
-    if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-  }
+  if (plan.ksplit > 1)
+    GRINQH_RETURN_IF(bind_workspace(workspace, plan.partial_bytes, plan.counter_bytes, zeroed, stream, &a.partial,
+                                    &a.counters));
   return launch_decode(a, plan, km, dtype, max_bits / 2, stream);
 }
 

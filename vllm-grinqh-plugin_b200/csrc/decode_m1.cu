@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "decode_m1.cuh"
+#include "ptx.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -210,7 +211,22 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   float* wacc = red + warp * kSliceN + kWpl * lane;  // this lane's columns: wacc[c * kSliceW + h]
 #pragma unroll
   for (int c = 0; c < 16; ++c) *reinterpret_cast<float2*>(wacc + c * kSliceW) = make_float2(0.f, 0.f);
+  // While an earlier kernel on the stream finishes (dependent launch), bring the planes
+  // of this warp's first rows into L2: the weights are never written by other kernels.
+  {
+    const int n16p = a.N >> 4, j0p = tile * kSliceW + kWpl * lane;
+    if (j0p < n16p && rb < re) {
+      const size_t rw = (size_t)NZ * n16p;
+#pragma unroll
+      for (int r = 0; r < kD; ++r)
+        if (rb + r < re)
+#pragma unroll
+          for (int z = 0; z < NZ; ++z) prefetch_l2(a.w + (size_t)(rb + r) * rw + (size_t)z * n16p + j0p);
+    }
+  }
+  wait_prior_grid();  // x and the outputs belong to the stream order from here on
   warp_chunk<NZ, T>(a, tile, rb, re, rows + (rb - k0), wacc);
+  allow_dependent_grid();
 
   // ---- sum the 8 warps' accumulators
   __syncthreads();
@@ -295,13 +311,17 @@ int launch_t(const M1Args& a, const M1Plan& p, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = (unsigned)p.cluster;
   attr[0].val.clusterDim.z = 1;
+  // may start while the previous kernel on the stream finishes (the kernel waits for
+  // it before touching x, the output or the workspace)
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "m1 GEMV launch: %s", cudaGetErrorString(e));
   return check_launch("m1 GEMV");

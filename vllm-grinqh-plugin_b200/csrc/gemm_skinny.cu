@@ -8,16 +8,17 @@
 // of 32 rows. Three rings of shared-memory stages:
 //   planes  (5 x 16 KB)  the b/2 plane words of 32 rows x 32 words, one 2-D TMA box
 //                        per plane (128-byte swizzle), loaded up to five steps ahead
-//                        by warp 16;
+//                        by warp 8;
 //   weights (4 x 32 KB)  operand A: dtype(w * s) for 512 columns x 32 rows, MN-major
 //                        with the 128-byte swizzle;
 //   x       (4 x 4 KB)   operand B: Mp x 32 activations, K-major with the 64-byte
 //                        swizzle (rows past M read as 0), loaded by TMA.
-// Warps 0-15 convert (a warp covers 8 rows x 4 word pairs, so that every shared-memory
-// access is free of bank conflicts): each thread owns two neighbouring words of one row, reads their
+// Warps 0-7 convert (a warp covers 8 rows x 4 word pairs twice, so that every
+// shared-memory access is free of bank conflicts): each thread owns two neighbouring
+// words of two rows 8 apart (same columns, same scales), reads their
 // planes from shared memory, merges them into codes, multiplies by the group scale,
 // rounds once to the activation dtype -- the reference's dtype(w * s), bit for bit --
-// and stores the weight stage; thread 0 also loads each step's x tile. Warp 17 issues
+// and stores the weight stage; thread 0 also loads each step's x tile. Warp 9 issues
 // the MMAs (per 16-deep K slice, one tcgen05.mma kind::f16 per 128-column block,
 // N = Mp) from one thread into TMEM; tcgen05.commit frees the stage. The converters
 // never wait on global memory: the plane ring hides its latency.
@@ -45,8 +46,8 @@ constexpr int TW = 32;         // packed words per tile
 constexpr int TN = 16 * TW;    // output columns per tile
 constexpr int BK = 32;         // rows per K step
 constexpr int SP = 5, SW = 4;  // plane stages; weight / activation stages
-constexpr int kConvWarps = 16;
-constexpr int kLoadWarp = 16, kMmaWarp = 17;
+constexpr int kConvWarps = 8;
+constexpr int kLoadWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = 32 * (kConvWarps + 2);
 constexpr int kMaxMp = 64;
 constexpr uint32_t kPlaneBytes = BK * TW * 4;  // one plane of a step: 4 KB
@@ -140,6 +141,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Dependent launch: only the plane loader may run ahead of the previous kernel on
+  // the stream (the weights are never written by other kernels); everything that
+  // reads x or writes the output or the workspace waits for it first.
+  const bool loader = warp == kLoadWarp && lane == 0;
+  if (!loader) wait_prior_grid();
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ plane loader
     if (lane == 0) {
@@ -153,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int z = 0; z < NZ; ++z)
           tma_load_2d(sP + s * kStageP + z * kPlaneBytes, &tmap_w, z * n16 + jt0, row, &p_full[s]);
       }
+      wait_prior_grid();
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -181,21 +188,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ converters
-    // a warp covers 8 rows x 4 word pairs: in every shared-memory access the 8 lanes of
-    // a phase are 8 different rows, which the 128-byte swizzle spreads over all banks
-    const int ct = threadIdx.x;                      // 0..511
-    const int rr = 8 * (warp & 3) + (lane & 7);      // row rr of each step
-    const int jp = 4 * (warp >> 2) + (lane >> 3);    // this thread's words: 2 jp, 2 jp + 1
+    // a warp covers 8 rows x 4 word pairs, twice: in every shared-memory access the 8
+    // lanes of a phase are 8 different rows, which the 128-byte swizzle spreads over
+    // all banks
+    const int ct = threadIdx.x;                      // 0..255
+    const int rr = 16 * (warp & 1) + (lane & 7);     // rows rr and rr + 8 of each step
+    const int jp = 4 * (warp >> 1) + (lane >> 3);    // this thread's words: 2 jp, 2 jp + 1
     const int jw = jt0 + 2 * jp;
     const bool jvalid = jw < n16;      // n16 is even: both words are valid or neither
     const int spg = a.group / BK;      // K steps per scale group
     const bool x_issuer = ct == 0;
     if (x_issuer) prefetch_tmap(&tmap_x);
     const uint32_t xbytes = (uint32_t)mp * BK * 2;
+    // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
+    // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u
+    constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
+    constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
     // scales of column group c for the two words, s[g, c * n16 + jw .. jw + 1] (the
     // 2^-shift of the shifted codes is in the magic constant below); the next group's
     // are prefetched as packed dtype pairs
-    float2 sreg[16];
+    float2 sreg[16], sneg[16];  // s and -(2^23 + 128) * s / 2^shift per column group
     uint32_t snext[16];
     auto load_scales = [&](int g) {
       const uint32_t* sp =
@@ -207,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         sreg[c] = Fmt<T>::unpack(snext[c]);
+        sneg[c] = make_float2(-kMagic * sreg[c].x, -kMagic * sreg[c].y);
       }
     };
     if (nq > 0) {
@@ -215,15 +228,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       unpack_scales();
       if ((g0 + 1) * spg < q0 + nq) load_scales(g0 + 1);
     }
-    // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
-    // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u
-    constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
-    constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
-    // store offsets of row rr in the weight stage (MN-major, 128-byte swizzle: 16-byte
-    // chunk c of row k sits at (c ^ (k & 7)))
+    // store offsets of rows rr, rr + 8 in the weight stage (MN-major, 128-byte swizzle:
+    // 16-byte chunk c of row k sits at (c ^ (k & 7)); both rows have k & 7 = rr & 7)
     const uint32_t rsw = (uint32_t)(rr & 7);
     const uint32_t c0 = (uint32_t)(4 * jp) & 7u;  // first of the thread's four chunks (0 or 4)
-    const uint32_t row_base = (uint32_t)(((4 * jp) >> 3) * kLbo + (rr >> 3) * kSbo + (rr & 7) * 128);
+    uint32_t row_base[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int k = rr + 8 * h;
+      row_base[h] = (uint32_t)(((4 * jp) >> 3) * kLbo + (k >> 3) * kSbo + (k & 7) * 128);
+    }
     uint32_t chunk_off[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) chunk_off[e] = ((c0 + (uint32_t)e) ^ rsw) << 4;
@@ -241,22 +255,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sX + s * kStageX, &tmap_x, q * BK, 0, &x_full[s]);
       }
       mbar_wait(&p_full[ps], (i / SP) & 1);
-      // plane words of the two words of row rr (the planes are 128-byte swizzled by the
-      // TMA: 16-byte chunk c of row r sits at chunk c ^ (r & 7))
-      uint2 P[4];
+      // plane words of the two words of rows rr, rr + 8 (the planes are 128-byte
+      // swizzled by the TMA: 16-byte chunk c of row r sits at chunk c ^ (r & 7))
+      uint2 P[2][4];
       const unsigned char* pst =
           sP + ps * kStageP + rr * (TW * 4) + ((((uint32_t)jp >> 1) ^ (uint32_t)(rr & 7)) << 4) + (jp & 1) * 8;
 #pragma unroll
-      for (int z = 0; z < 4; ++z)
-        P[z] = z < NZ ? *reinterpret_cast<const uint2*>(pst + z * kPlaneBytes) : make_uint2(0u, 0u);
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+          P[h][z] = z < NZ ? *reinterpret_cast<const uint2*>(pst + h * 8 * (TW * 4) + z * kPlaneBytes)
+                           : make_uint2(0u, 0u);
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_empty[ps]);
 
       unsigned char* wst = sW + s * kStageW;
-      {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
         uint32_t qa[4], qb[4];  // merged code bytes of word 2 jp (a) and 2 jp + 1 (b)
-        merge_planes(P[0].x ^ kSignFlip, P[1].x, P[2].x, P[3].x, qa);
-        merge_planes(P[0].y ^ kSignFlip, P[1].y, P[2].y, P[3].y, qb);
+        merge_planes(P[h][0].x ^ kSignFlip, P[h][1].x, P[h][2].x, P[h][3].x, qa);
+        merge_planes(P[h][0].y ^ kSignFlip, P[h][1].y, P[h][2].y, P[h][3].y, qb);
         uint32_t oa[8], ob[8];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -266,13 +284,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t sel = 0x7440u | (uint32_t)L;
             const float2 f = make_float2(__int_as_float(__byte_perm(qa[t], kMagicBits, sel)),
                                          __int_as_float(__byte_perm(qb[t], kMagicBits, sel)));
-            const float2 sc = sreg[4 * t + L];
             if constexpr (Fmt<T>::v == 1) {
               // bf16 scale (8 significant bits): (2^23 + 128) * s / 2^shift is exact in
               // fp32, so one fused multiply-add gives code * s exactly
-              v[L] = __ffma2_rn(f, sc, make_float2(-kMagic * sc.x, -kMagic * sc.y));
+              v[L] = __ffma2_rn(f, sreg[4 * t + L], sneg[4 * t + L]);
             } else {
-              v[L] = __fmul2_rn(__fadd2_rn(f, make_float2(-kMagic, -kMagic)), sc);
+              v[L] = __fmul2_rn(__fadd2_rn(f, make_float2(-kMagic, -kMagic)), sreg[4 * t + L]);
             }
           }
           // code * s exactly in fp32, rounded once to the activation dtype (kernel.py:586)
@@ -281,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ob[2 * t] = Fmt<T>::pack(v[0].y, v[1].y);
           ob[2 * t + 1] = Fmt<T>::pack(v[2].y, v[3].y);
         }
-        unsigned char* rowp = wst + row_base;
+        unsigned char* rowp = wst + row_base[h];
         *reinterpret_cast<uint4*>(rowp + chunk_off[0]) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
         *reinterpret_cast<uint4*>(rowp + chunk_off[1]) = make_uint4(oa[4], oa[5], oa[6], oa[7]);
         *reinterpret_cast<uint4*>(rowp + chunk_off[2]) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
@@ -292,6 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&w_full[s]);
     }
 
+    allow_dependent_grid();
+
     // ------------------------------------------------------------ partial tile -> smem
     // accumulator block b, TMEM lane p (this warp may read lanes 32 * (warp % 4) ..):
     // tile position P = 128 b + p, word P / 16, column group P % 16 (the converters'
@@ -300,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     float* part = reinterpret_cast<float*>(smem);  // the stages are idle now
     const int quarter = warp & 3;
-    {
-      const int blk = warp >> 2;
+#pragma unroll 1
+    for (int blk = warp >> 2; blk < 4; blk += 2) {
       const int pos = blk * 128 + quarter * 32 + lane;
       const int pw = pos >> 4, pc = pos & 15;
       for (int h = 0; h < (int)cstride; h += 32) {
@@ -430,13 +449,15 @@ int launch_t(const SkinnyArgs& a, const SkinnyPlan& p, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = (unsigned)p.cluster;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see wait_prior_grid()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, tmap_x, tmap_w, a, p.mp);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "skinny GEMM launch: %s", cudaGetErrorString(e));
   return check_launch("skinny GEMM");

@@ -111,6 +111,19 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel on the stream finishes. It must
+// wait before reading anything that kernel writes (or writing anything it reads);
+// without the launch attribute both instructions do nothing.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_grid() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // ---------------------------------------------------------------- predicated loads
 // v = (mask & bit) ? *p : 0, streaming (evict-first) global load
 __device__ __forceinline__ uint32_t ld_cs_if(const uint32_t* p, uint32_t mask, uint32_t bit) {

@@ -11,8 +11,12 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
 #include <optional>
+#include <utility>
 #include <vector>
 
 #include "grinqh_b200.h"
@@ -47,6 +51,34 @@ std::vector<float> thresholds4(at::ArrayRef<double> th) {
 
 cudaStream_t cur_stream(const at::Tensor& t) {
   return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+// A zeroed workspace per (device, stream), grown on demand and kept for the process.
+// The kernels leave their split-K tickets at zero, so a call that reuses it passes
+// GRINQH_WORKSPACE_ZEROED and no clearing runs on the stream; calls on one stream are
+// ordered, and other streams get their own. A workspace is only created outside
+// stream capture (a capture records the zeroing instead of running it): a call
+// captured before any eager call on its stream allocates per call as before.
+at::Tensor stream_workspace(const at::Tensor& like, size_t bytes, cudaStream_t st, bool* zeroed) {
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, at::Tensor> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(static_cast<int>(like.device().index()), reinterpret_cast<uintptr_t>(st));
+  auto it = cache.find(key);
+  if (it != cache.end() && static_cast<size_t>(it->second.numel()) >= bytes) {
+    *zeroed = true;
+    return it->second;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    *zeroed = false;
+    return at::empty({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+  }
+  const size_t size = std::max<size_t>(bytes, size_t(1) << 20);
+  at::Tensor t = at::zeros({static_cast<int64_t>(size)}, like.options().dtype(at::kByte));
+  cache[key] = t;
+  *zeroed = true;
+  return t;
 }
 
 int env_mode_for_rows() {
@@ -96,12 +128,15 @@ at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, cons
   if (M == 0) return y.view(out_shape);
   const auto th = thresholds4(thresholds);
   const size_t ws_bytes = grinqh_workspace_size(M, K, N, (int)max_bits, (int)group_size, mode);
+  const cudaStream_t stream = cur_stream(x);
   at::Tensor ws;
-  if (ws_bytes) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
+  bool zeroed = false;
+  if (ws_bytes) ws = stream_workspace(x, ws_bytes, stream, &zeroed);
+  const int call_mode = zeroed ? (mode | GRINQH_WORKSPACE_ZEROED) : mode;
   const int st = grinqh_gemm_or_gemv(xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()),
                                      sc.data_ptr(), bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N,
-                                     th.data(), mode, y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
-                                     cur_stream(x));
+                                     th.data(), call_mode, y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr,
+                                     ws_bytes ? static_cast<size_t>(ws.numel()) : 0, stream);
   check_ok(st, "gemm_or_gemv");
   return y.view(out_shape);
 }
