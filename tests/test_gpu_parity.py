@@ -371,15 +371,17 @@ def test_dense_tensor_core_gemm(M, K, N, dtype, b):
     assert_parity(f32(y), O.to_f32(ref, dtype))
 
 
-@pytest.mark.parametrize("M,K,N", [(2, 256, 256), (5, 384, 320), (16, 4096, 1024), (17, 1024, 4112),
-                                   (33, 2048, 6144), (48, 512, 528), (64, 8192, 512)])
+@pytest.mark.parametrize("M,K,N", [(2, 256, 256), (5, 384, 320), (16, 4096, 1024), (17, 1024, 4128),
+                                   (33, 2048, 6144), (48, 512, 544), (64, 8192, 512), (17, 1024, 4112),
+                                   (48, 512, 528)])
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("b", [8, 4, 2, 6])
 def test_dense_skinny_gemm(M, K, N, dtype, b):
     """Rows 2..64 run the skinny tcgen05 GEMM (weights as operand A, tokens as N): a
-    single K split (2 x 256 x 256), clusters with one sum (5 x 384 x 320), several
-    clusters per tile (16 x 4096 x 1024: 64 splits in clusters of 8), partial column
-    tiles (N/16 = 257, 33), padded token counts (17, 33, 48) and the largest count (64)."""
+    single cluster (2 x 256 x 256, 5 x 384 x 320), several clusters per tile
+    (16 x 4096 x 1024: 64 splits in clusters of 8), partial column tiles (N/16 = 258,
+    34), padded token counts (17, 33, 48) and the largest count (64). N/16 odd (4112,
+    528) falls back to the generic kernel."""
     from grinqh.kernel import grinqh_gemm_or_gemv
     from grinqh.utils import pack_codes
     rng = np.random.default_rng(M * 31 + K + N + b)
@@ -399,3 +401,27 @@ def test_dense_skinny_gemm(M, K, N, dtype, b):
     y2 = grinqh_gemm_or_gemv(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128,
                              N // 4, [0.0] * 4)
     assert torch.equal(y, y2), "skinny GEMM is not deterministic"
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 256, 4112), (600, 384, 320), (1024, 1024, 1024)])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("b", [8, 4, 2, 6])
+def test_dense_two_pass_gemm(M, K, N, dtype, b):
+    """Rows >= 512 dequantize once to dtype(w*s) and run the TMA-fed tcgen05 GEMM: a
+    partial last column tile (N = 4112), a row tail (600) and several tiles each way."""
+    from grinqh.kernel import grinqh_gemm_or_gemv
+    from grinqh.utils import pack_codes
+    rng = np.random.default_rng(M + 3 * K + N + b)
+    lim = 1 << (b - 1)
+    codes = rng.integers(-lim, lim, size=(K, N)).astype(np.int8)
+    s32 = (rng.random((K // 128, N)) * 0.02 + 0.001).astype(np.float32)
+    s_store = O.round_to_dtype(s32, dtype)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    xs = O.round_to_dtype(x, dtype)
+    bias = O.round_to_dtype(rng.standard_normal(N).astype(np.float32), dtype)
+    w = pack_codes(torch.from_numpy(codes).cuda(), b)
+    y = grinqh_gemm_or_gemv(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128,
+                            N // 4, [0.0] * 4)
+    ref = O.gemm_or_gemv(O.to_f32(xs, dtype), codes, O.to_f32(s_store, dtype), O.to_f32(bias, dtype), b, 128,
+                         [0.0] * 4, dtype)
+    assert_parity(f32(y), O.to_f32(ref, dtype))

@@ -9,6 +9,7 @@
 #include "gemm_tc.cuh"
 #include "decode_tc.cuh"
 #include "gemm_skinny.cuh"
+#include "gemm_bf16.cuh"
 
 namespace grinqh {
 
@@ -129,12 +130,20 @@ static bool use_m1tc(int kmode, int64_t M, int64_t K, int64_t N, int group) {
 
 // Dense rows up to this count run the skinny tcgen05 GEMM (weights as operand A).
 constexpr int64_t kSkinnyMaxRows = 64;
+// From this many dense rows the weights are dequantized once per call to dtype(w * s)
+// and multiplied by the TMA-fed tcgen05 GEMM (gemm_bf16.cu); between the two, the
+// fused tcgen05 GEMM (gemm_tc.cu) converts planes in its converter warps.
+constexpr int64_t kBf16MinRows = 512;
 
 // Kernel choice: graded / union rows of one token use the register-streaming
 // single-row kernel; dense rows 2..kSkinnyMaxRows the skinny tcgen05 GEMM; dense
 // rows above that the tcgen05 GEMM; everything else the generic small-M kernel.
 static bool use_m1(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return (kmode == kModeGraded || kmode == kModeUnion) && m1_supported(M, K, N, group);
+}
+
+static bool use_bf16_gemm(int kmode, int64_t M, int64_t K, int64_t N) {
+  return kmode == kModeDense && M >= kBf16MinRows && K % 64 == 0 && N % 16 == 0;
 }
 
 static bool use_skinny(int kmode, int64_t M, int64_t K, int64_t N, int group) {
@@ -196,6 +205,11 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   // an activation or output view that the tensor-core kernels cannot take (alignment)
   // runs the generic kernel, and this query does not see the pointers: cover both
   const size_t generic = workspace_for(plan_decode(M, K, N, km, sms));
+  if (use_bf16_gemm(km, M, K, N)) {
+    // the dtype(w * s) buffer sits after the ticket region, which it never touches
+    const size_t a = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
+    return a > generic ? a : generic;
+  }
   if (use_skinny(km, M, K, N, group_size)) {
     const size_t a = workspace_for(plan_skinny(M, K, N, sms));
     return a > generic ? a : generic;
@@ -289,6 +303,25 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_skinny(g, plan, dtype, max_bits / 2, stream);
   }
 
+  if (use_bf16_gemm(km, M, K, N) && bf16_gemm_supported(M, K, N, group, x, y)) {
+    const size_t need = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    Bf16GemmArgs g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.wbuf = static_cast<char*>(workspace) + kTicketBytes;
+    g.M = (int)M;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    return launch_bf16_gemm(g, dtype, max_bits / 2, stream);
+  }
+
   if (km == kModeDense && M > kSkinnyMaxRows && gemm_tc_supported(M, K, N, group, x, y)) {
     GemmArgs g{};
     g.x = x;
@@ -330,7 +363,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
   GRINQH_RETURN_IF(check_device());
-  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts() + take_skinny_timeouts();
+  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts() + take_skinny_timeouts() + take_bf16_gemm_timeouts();
   if (timeouts) *timeouts = v;
   return GRINQH_OK;
 }

@@ -1,0 +1,293 @@
+// Dense quantized GEMM for many rows in two passes, the reference's structure
+// (grinqh/kernel.py:561-587: unpack, dtype(w * s), x @ w) with both passes on this
+// library's kernels:
+//   1. dequant_kernel turns the packed planes into W = dtype(w * s) [K, N] in the
+//      original column order (HBM-bound: b/8 bytes read, 2 written per weight);
+//   2. gemm_bf16_kernel computes y = x @ W on the tcgen05 tensor cores with both
+//      operands loaded by TMA: warp 0 loads a 256 x 64 x tile (K-major) and four
+//      64 x 64 boxes of W (128-byte swizzle, which is the MN-major operand layout)
+//      per stage, warp 1 issues the MMAs from one thread (two M = 128 halves,
+//      N = 256), warps 2-9 are the epilogue (tcgen05.ld, cast, bias, store).
+// For many rows the dequantization is paid once per call while the fused kernel
+// (gemm_tc.cu) converts every weight once per 256-row tile of x; above a few hundred
+// rows the separate pass is cheaper. Both give dtype(w * s) bit for bit.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm_bf16.cuh"
+#include "ptx.cuh"
+
+namespace grinqh {
+namespace {
+
+constexpr int BM = 256, BN = 256, BK = 64, STAGES = 3;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr uint32_t kStageA = BM * BK * 2;  // 32 KB
+constexpr uint32_t kStageB = BN * BK * 2;  // 32 KB
+constexpr uint32_t kBoxB = 64 * BK * 2;    // one 64-column box of W: 8 KB
+constexpr uint32_t kSmemBytes = STAGES * (kStageA + kStageB) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kLboB = 8 * 1024;  // B: stride between 64-column MN atoms
+constexpr uint32_t kSboB = 1024;      // B: stride between 8-row K groups
+constexpr uint32_t kSboA = 1024;      // A: stride between 8-row M groups (128 B rows)
+
+template <typename T> struct Fmt;
+template <> struct Fmt<__nv_bfloat16> {
+  static constexpr uint32_t v = 1;
+  static constexpr CUtensorMapDataType tma = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+};
+template <> struct Fmt<__half> {
+  static constexpr uint32_t v = 0;
+  static constexpr CUtensorMapDataType tma = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+};
+
+// ---------------------------------------------------------------- pass 1: dequantize
+// Thread (k, j): the b/2 plane words of packed word j of row k hold the 16 codes of
+// columns c * N/16 + j (c = 0..15); W[k, c * N/16 + j] = dtype(code * s[k / group, .]).
+template <int NZ, typename T>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint32_t* __restrict__ w, const T* __restrict__ s,
+                                                      T* __restrict__ out, int K, int N, int group) {
+  constexpr int kShift = 8 - 2 * NZ;
+  // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
+  // 2^(23-shift) exactly: the float with bits 0x4B000000 - (shift << 23) | u
+  constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
+  constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
+  const int n16 = N >> 4;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n16) return;
+  const size_t row_words = (size_t)NZ * n16;
+  for (int k = blockIdx.y; k < K; k += gridDim.y) {
+    uint32_t P[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z) P[z] = z < NZ ? __ldcs(w + (size_t)k * row_words + (size_t)z * n16 + j) : 0u;
+    uint32_t q[4];
+    merge_planes(P[0] ^ kSignFlip, P[1], P[2], P[3], q);
+    const T* srow = s + (size_t)(k / group) * N + j;
+    T* orow = out + (size_t)k * N + j;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int L = 0; L < 4; ++L) {
+        const int c = 4 * i + L;
+        const float sc = Act<T>::to_f(srow[(size_t)c * n16]);
+        const float f = __int_as_float(__byte_perm(q[i], kMagicBits, 0x7440u | (uint32_t)L));
+        // code * s exactly in fp32 (for bf16 scales (2^23 + 128) * s / 2^shift is exact,
+        // so the fused multiply-add is exact; for fp16, f - magic is exact first), then
+        // rounded once to the activation dtype (kernel.py:586)
+        const float v = Fmt<T>::v == 1 ? fmaf(f, sc, -kMagic * sc) : (f - kMagic) * sc;
+        orow[(size_t)c * n16] = Act<T>::from_f(v);
+      }
+  }
+}
+
+// ---------------------------------------------------------------- pass 2: x @ W
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                  const __grid_constant__ CUtensorMap tmap_w,
+                                                                  const Bf16GemmArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = smem;
+  unsigned char* sB = smem + STAGES * kStageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * (kStageA + kStageB));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  const int nk = a.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      prefetch_tmap(&tmap_w);
+      for (int q = 0; q < nk; ++q) {
+        const int s = q % STAGES;
+        if (q >= STAGES) mbar_wait(&empty[s], ((q / STAGES) - 1) & 1);
+        mbar_arrive_expect_tx(&full[s], kStageA + kStageB);
+        tma_load_2d(sA + s * kStageA, &tmap_x, q * BK, m0, &full[s]);
+#pragma unroll
+        for (int b = 0; b < BN / 64; ++b) tma_load_2d(sB + s * kStageB + b * kBoxB, &tmap_w, n0 + 64 * b, q * BK, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(1, Fmt<T>::v, Fmt<T>::v, 0, 1, BN, 128);
+      for (int q = 0; q < nk; ++q) {
+        const int s = q % STAGES;
+        mbar_wait(&full[s], (q / STAGES) & 1);
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA + s * kStageA);
+        const uint32_t b_base = smem_u32(sB + s * kStageB);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t bdesc = smem_desc(b_base + kk * 2 * kSboB, kLboB, kSboB, 2);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t adesc = smem_desc(a_base + h * 128 * 128 + kk * 32, 16, kSboA, 2);
+            mma_f16_ss(tmem + h * BN, adesc, bdesc, idesc, (q > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&empty[s]);
+      }
+      mma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // warp w reads TMEM lanes 32 * (w % 4) .. of accumulator half (w - 2) / 4: each
+    // thread owns one output row and writes it in 64-byte runs of 32 columns
+    mbar_wait(acc_full, 0);
+    tc_fence_after();
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int m = m0 + half * 128 + quarter * 32 + lane;
+    T* y = static_cast<T*>(a.y);
+    const T* bias = static_cast<const T*>(a.bias);
+#pragma unroll 1
+    for (int cc = 0; cc < BN / 32; ++cc) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + half * BN + cc * 32, r);
+      tmem_ld_wait();
+      if (m >= a.M) continue;
+      const int nb = n0 + 32 * cc;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {  // 8 columns (16 bytes) at a time
+        const int n = nb + 8 * e;
+        if (n >= a.N) break;  // N is a multiple of 16, so runs of 8 are whole
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          T lo = Act<T>::from_f(__uint_as_float(r[8 * e + 2 * t]));
+          T hi = Act<T>::from_f(__uint_as_float(r[8 * e + 2 * t + 1]));
+          if (bias) {
+            lo = Act<T>::from_f(Act<T>::to_f(lo) + Act<T>::to_f(bias[n + 2 * t]));
+            hi = Act<T>::from_f(Act<T>::to_f(hi) + Act<T>::to_f(bias[n + 2 * t + 1]));
+          }
+          o[t] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+        }
+        *reinterpret_cast<uint4*>(y + (size_t)m * a.N + n) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+template <int NZ, typename T>
+int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
+  // pass 1
+  {
+    const int n16 = a.N / 16;
+    const dim3 grid((unsigned)((n16 + 255) / 256), (unsigned)(a.K < 4096 ? a.K : 4096));
+    dequant_kernel<NZ, T><<<grid, 256, 0, st>>>(a.w, static_cast<const T*>(a.s), static_cast<T*>(a.wbuf), a.K, a.N,
+                                                a.group);
+    GRINQH_RETURN_IF(check_launch("dequant"));
+  }
+  // pass 2
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint32_t estride[2] = {1, 1};
+  CUtensorMap tmap_x, tmap_w;
+  {
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+    const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
+    const cuuint32_t box[2] = {BK, BM};
+    const CUresult r = enc(&tmap_x, Fmt<T>::tma, 2, const_cast<void*>(a.x), gdim, gstride, box, estride,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed (%d)", (int)r);
+  }
+  {
+    // W [K, N]: boxes of 64 columns (128 bytes) x 64 rows with the 128-byte swizzle,
+    // which is the MN-major operand layout (8-row K groups of 1 KB, 64-column atoms)
+    const cuuint64_t gdim[2] = {(cuuint64_t)a.N, (cuuint64_t)a.K};
+    const cuuint64_t gstride[1] = {(cuuint64_t)a.N * 2};
+    const cuuint32_t box[2] = {64, BK};
+    const CUresult r = enc(&tmap_w, Fmt<T>::tma, 2, a.wbuf, gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed (%d)", (int)r);
+  }
+  auto kern = gemm_bf16_kernel<T>;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  const dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN));
+  kern<<<grid, kThreads, kSmemBytes, st>>>(tmap_x, tmap_w, a);
+  return check_launch("gemm_bf16");
+}
+
+}  // namespace
+
+unsigned take_bf16_gemm_timeouts() {
+  unsigned v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess) return 0;
+  cudaMemcpyToSymbol(g_wait_timeouts, &z, sizeof(z));
+  return v;
+}
+
+bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* y) {
+  // TMA needs 16-byte aligned bases and row pitches (K, N multiples of 8), whole 64-deep
+  // K steps; the epilogue stores 16-byte runs (N a multiple of 16, y 16-byte aligned)
+  (void)group;
+  return M >= 1 && K % BK == 0 && N % 16 == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(y) % 16) == 0 && K < (1LL << 31) && N < (1LL << 31);
+}
+
+size_t bf16_gemm_buffer_bytes(int64_t K, int64_t N) { return (size_t)K * (size_t)N * 2; }
+
+int launch_bf16_gemm(const Bf16GemmArgs& a, int dtype, int nz, cudaStream_t st) {
+  if (dtype == GRINQH_BF16) {
+    switch (nz) {
+      case 1: return launch_t<1, __nv_bfloat16>(a, st);
+      case 2: return launch_t<2, __nv_bfloat16>(a, st);
+      case 3: return launch_t<3, __nv_bfloat16>(a, st);
+      default: return launch_t<4, __nv_bfloat16>(a, st);
+    }
+  }
+  switch (nz) {
+    case 1: return launch_t<1, __half>(a, st);
+    case 2: return launch_t<2, __half>(a, st);
+    case 3: return launch_t<3, __half>(a, st);
+    default: return launch_t<4, __half>(a, st);
+  }
+}
+
+}  // namespace grinqh
