@@ -403,12 +403,13 @@ def test_dense_skinny_gemm(M, K, N, dtype, b):
     assert torch.equal(y, y2), "skinny GEMM is not deterministic"
 
 
-@pytest.mark.parametrize("M,K,N", [(512, 256, 4112), (600, 384, 320), (1024, 1024, 1024)])
+@pytest.mark.parametrize("M,K,N", [(512, 256, 4128), (600, 384, 320), (1024, 1024, 1024), (520, 256, 4112)])
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("b", [8, 4, 2, 6])
 def test_dense_two_pass_gemm(M, K, N, dtype, b):
     """Rows >= 512 dequantize once to dtype(w*s) and run the TMA-fed tcgen05 GEMM: a
-    partial last column tile (N = 4112), a row tail (600) and several tiles each way."""
+    partial last column tile (N = 4128), a row tail (600) and several tiles each way;
+    N/16 odd (4112) takes the fused GEMM instead."""
     from grinqh.kernel import grinqh_gemm_or_gemv
     from grinqh.utils import pack_codes
     rng = np.random.default_rng(M + 3 * K + N + b)

@@ -130,10 +130,11 @@ static bool use_m1tc(int kmode, int64_t M, int64_t K, int64_t N, int group) {
 
 // Dense rows up to this count run the skinny tcgen05 GEMM (weights as operand A).
 constexpr int64_t kSkinnyMaxRows = 64;
-// From this many dense rows the weights are dequantized once per call to dtype(w * s)
-// and multiplied by the TMA-fed tcgen05 GEMM (gemm_bf16.cu); between the two, the
-// fused tcgen05 GEMM (gemm_tc.cu) converts planes in its converter warps.
-constexpr int64_t kBf16MinRows = 512;
+// Above the skinny range the weights are dequantized once per call to dtype(w * s) and
+// multiplied by the TMA-fed tcgen05 GEMM (gemm_bf16.cu); the fused tcgen05 GEMM
+// (gemm_tc.cu, planes converted in its converter warps) takes the shapes that path
+// cannot (N / 16 odd, unaligned views).
+constexpr int64_t kBf16MinRows = kSkinnyMaxRows + 1;
 
 // Kernel choice: graded / union rows of one token use the register-streaming
 // single-row kernel; dense rows 2..kSkinnyMaxRows the skinny tcgen05 GEMM; dense
@@ -142,8 +143,13 @@ static bool use_m1(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return (kmode == kModeGraded || kmode == kModeUnion) && m1_supported(M, K, N, group);
 }
 
-static bool use_bf16_gemm(int kmode, int64_t M, int64_t K, int64_t N) {
-  return kmode == kModeDense && M >= kBf16MinRows && K % 64 == 0 && N % 16 == 0;
+// The dequantization pass costs about as much as streaming the weights three times, so
+// it pays off with many rows, or when the fused GEMM's 256 x 256 tiles would leave more
+// than half of the SMs idle.
+static bool use_bf16_gemm(int kmode, int64_t M, int64_t K, int64_t N, int sms) {
+  if (kmode != kModeDense || M < kBf16MinRows || K % 64 != 0 || N % 32 != 0) return false;
+  const int64_t fused_ctas = ((M + 255) / 256) * ((N / 16 + 15) / 16);
+  return M >= 512 || fused_ctas < sms / 2;
 }
 
 static bool use_skinny(int kmode, int64_t M, int64_t K, int64_t N, int group) {
@@ -205,7 +211,7 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   // an activation or output view that the tensor-core kernels cannot take (alignment)
   // runs the generic kernel, and this query does not see the pointers: cover both
   const size_t generic = workspace_for(plan_decode(M, K, N, km, sms));
-  if (use_bf16_gemm(km, M, K, N)) {
+  if (use_bf16_gemm(km, M, K, N, sms)) {
     // the dtype(w * s) buffer sits after the ticket region, which it never touches
     const size_t a = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
     return a > generic ? a : generic;
@@ -303,7 +309,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_skinny(g, plan, dtype, max_bits / 2, stream);
   }
 
-  if (use_bf16_gemm(km, M, K, N) && bf16_gemm_supported(M, K, N, group, x, y)) {
+  if (use_bf16_gemm(km, M, K, N, sms) && bf16_gemm_supported(M, K, N, group, x, w, s, y)) {
     const size_t need = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);

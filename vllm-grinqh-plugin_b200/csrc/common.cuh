@@ -37,12 +37,14 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 // ------------------------------------------------------------------ dtype traits
 template <typename T> struct Act;
 template <> struct Act<__nv_bfloat16> {
+  static constexpr bool kBf16 = true;
   static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
   // round a float to the activation dtype and back (torch's w.to(dtype) * s rounding)
   static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 };
 template <> struct Act<__half> {
+  static constexpr bool kBf16 = false;
   static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
   static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
   static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }

@@ -43,8 +43,13 @@ template <> struct Fmt<__half> {
 };
 
 // ---------------------------------------------------------------- pass 1: dequantize
-// Thread (k, j): the b/2 plane words of packed word j of row k hold the 16 codes of
-// columns c * N/16 + j (c = 0..15); W[k, c * N/16 + j] = dtype(code * s[k / group, .]).
+// Thread (chunk, pair): packed words 2p, 2p + 1 of kDqRows consecutive rows inside one
+// scale group. The b/2 plane words of word j of row k hold the 16 codes of columns
+// c * N/16 + j (c = 0..15), so the two words give, for every c, two neighbouring
+// columns: one packed store per column pair, and the group's scales are loaded once
+// as pairs. W[k, n] = dtype(code * s[k / group, n]).
+constexpr int kDqRows = 8;
+
 template <int NZ, typename T>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint32_t* __restrict__ w, const T* __restrict__ s,
                                                       T* __restrict__ out, int K, int N, int group) {
@@ -53,30 +58,66 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint32_t* __restrict
   // 2^(23-shift) exactly: the float with bits 0x4B000000 - (shift << 23) | u
   constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
   constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
-  const int n16 = N >> 4;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= n16) return;
+  const int n16 = N >> 4;          // even (N % 32 == 0)
+  const int pairs = n16 >> 1;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= pairs) return;
+  const int j = 2 * p;
+  const int k0 = blockIdx.y * kDqRows;
+  if (k0 >= K) return;
+  const int k1 = min(K, k0 + kDqRows);  // kDqRows divides the group: one scale group
   const size_t row_words = (size_t)NZ * n16;
-  for (int k = blockIdx.y; k < K; k += gridDim.y) {
-    uint32_t P[4];
+  // scales of the two columns of every column group, and the exact fused-multiply-add
+  // addends -(2^23 + 128) * s / 2^shift (bf16 scales have 8 significant bits)
+  float2 sc[16], sn[16];
+  {
+    const uint32_t* sp = reinterpret_cast<const uint32_t*>(s + (size_t)(k0 / group) * N + j);
 #pragma unroll
-    for (int z = 0; z < 4; ++z) P[z] = z < NZ ? __ldcs(w + (size_t)k * row_words + (size_t)z * n16 + j) : 0u;
-    uint32_t q[4];
-    merge_planes(P[0] ^ kSignFlip, P[1], P[2], P[3], q);
-    const T* srow = s + (size_t)(k / group) * N + j;
-    T* orow = out + (size_t)k * N + j;
+    for (int c = 0; c < 16; ++c) {
+      const uint32_t bits = __ldg(sp + (size_t)c * (n16 >> 1));
+      if constexpr (Act<T>::kBf16) {
+        sc[c] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bits));
+      } else {
+        sc[c] = __half22float2(*reinterpret_cast<const __half2*>(&bits));
+      }
+      sn[c] = make_float2(-kMagic * sc[c].x, -kMagic * sc[c].y);
+    }
+  }
+  const uint32_t* wp = w + (size_t)k0 * row_words + j;
+  T* op = out + (size_t)k0 * N + j;
+#pragma unroll 2
+  for (int k = k0; k < k1; ++k, wp += row_words, op += N) {
+    uint2 P[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z)
+      P[z] = z < NZ ? __ldcs(reinterpret_cast<const uint2*>(wp + (size_t)z * n16)) : make_uint2(0u, 0u);
+    uint32_t qa[4], qb[4];
+    merge_planes(P[0].x ^ kSignFlip, P[1].x, P[2].x, P[3].x, qa);
+    merge_planes(P[0].y ^ kSignFlip, P[1].y, P[2].y, P[3].y, qb);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int L = 0; L < 4; ++L) {
         const int c = 4 * i + L;
-        const float sc = Act<T>::to_f(srow[(size_t)c * n16]);
-        const float f = __int_as_float(__byte_perm(q[i], kMagicBits, 0x7440u | (uint32_t)L));
-        // code * s exactly in fp32 (for bf16 scales (2^23 + 128) * s / 2^shift is exact,
-        // so the fused multiply-add is exact; for fp16, f - magic is exact first), then
-        // rounded once to the activation dtype (kernel.py:586)
-        const float v = Fmt<T>::v == 1 ? fmaf(f, sc, -kMagic * sc) : (f - kMagic) * sc;
-        orow[(size_t)c * n16] = Act<T>::from_f(v);
+        const uint32_t sel = 0x7440u | (uint32_t)L;
+        const float2 f = make_float2(__int_as_float(__byte_perm(qa[i], kMagicBits, sel)),
+                                     __int_as_float(__byte_perm(qb[i], kMagicBits, sel)));
+        // code * s exactly in fp32, rounded once to the activation dtype (kernel.py:586)
+        float2 v;
+        if constexpr (Act<T>::kBf16) {
+          v = __ffma2_rn(f, sc[c], sn[c]);
+        } else {
+          v = __fmul2_rn(__fadd2_rn(f, make_float2(-kMagic, -kMagic)), sc[c]);
+        }
+        uint32_t packed;
+        if constexpr (Act<T>::kBf16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+          packed = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(v.x, v.y);
+          packed = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint32_t*>(op + (size_t)c * n16) = packed;
       }
   }
 }
@@ -215,9 +256,9 @@ template <int NZ, typename T>
 int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
   // pass 1
   {
-    const int n16 = a.N / 16;
-    const dim3 grid((unsigned)((n16 + 255) / 256), (unsigned)(a.K < 4096 ? a.K : 4096));
-    dequant_kernel<NZ, T><<<grid, 256, 0, st>>>(a.w, static_cast<const T*>(a.s), static_cast<T*>(a.wbuf), a.K, a.N,
+    const int pairs = a.N / 32;
+    const dim3 grid((unsigned)((pairs + 127) / 128), (unsigned)((a.K + kDqRows - 1) / kDqRows));
+    dequant_kernel<NZ, T><<<grid, 128, 0, st>>>(a.w, static_cast<const T*>(a.s), static_cast<T*>(a.wbuf), a.K, a.N,
                                                 a.group);
     GRINQH_RETURN_IF(check_launch("dequant"));
   }
@@ -263,11 +304,15 @@ unsigned take_bf16_gemm_timeouts() {
   return v;
 }
 
-bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* y) {
+bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* w, const void* s,
+                         const void* y) {
   // TMA needs 16-byte aligned bases and row pitches (K, N multiples of 8), whole 64-deep
   // K steps; the epilogue stores 16-byte runs (N a multiple of 16, y 16-byte aligned)
+  // the dequantization pass takes pairs of words (N % 32) and 32-row chunks of one
+  // scale group (group % 32, checked by the caller's validation)
   (void)group;
-  return M >= 1 && K % BK == 0 && N % 16 == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+  return M >= 1 && K % BK == 0 && N % 32 == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(w) % 8) == 0 && (reinterpret_cast<uintptr_t>(s) % 4) == 0 &&
          (reinterpret_cast<uintptr_t>(y) % 16) == 0 && K < (1LL << 31) && N < (1LL << 31);
 }
 

@@ -18,7 +18,8 @@ struct Bf16GemmArgs {
   int M, K, N, group;
 };
 
-bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* y);
+bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* w, const void* s,
+                         const void* y);
 size_t bf16_gemm_buffer_bytes(int64_t K, int64_t N);
 int launch_bf16_gemm(const Bf16GemmArgs& a, int dtype, int nz, cudaStream_t st);
 unsigned take_bf16_gemm_timeouts();
