@@ -119,8 +119,18 @@ static size_t workspace_for(const M1TcPlan& p) { return split_workspace(p.slot_b
 
 // The int8 tensor-core single-row kernel (decode_tc.cu) is selected only when
 // GRINQH_M1_TENSOR_CORES=1: it is exact but slower than the register-streaming
-// kernel on the Llama-3-8B shapes (gate_up 64 us vs 48 us at b = 8), so it is not
-// the default. The variable is read on every call (a getenv, no allocation).
+// kernel on the Llama-3-8B shapes (gate_up 44 us vs 36 us at b = 8, graded; both
+// are bound by the integer work of merging the 2-bit planes), so it is not the
+// default. The variable is read on every call (a getenv, no allocation).
+//
+// A unit's plane comes by TMA for all 64 rows when more than GRINQH_TC_TMA_ROWS
+// (default 0: always) of the rows need it, else by per-row cp.async of the graded
+// rows only; all-TMA measured fastest (gate_up 42 us vs 47-50 us for 16-48).
+static int tc_tma_min_rows() {
+  const char* e = getenv("GRINQH_TC_TMA_ROWS");
+  return e ? atoi(e) : 0;
+}
+
 static bool use_m1tc(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   const char* e = getenv("GRINQH_M1_TENSOR_CORES");
   if (!e || e[0] != '1') return false;
@@ -200,7 +210,14 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
-  if (use_m1tc(km, M, K, N, group_size)) return workspace_for(plan_m1tc(K, N, sms));
+  if (use_m1tc(km, M, K, N, group_size)) {
+    // a weight view that is not 16-byte aligned runs the streaming kernel: cover both
+    const size_t a = workspace_for(plan_m1tc(K, N, max_bits / 2, sms));
+    const size_t b = use_m1(km, M, K, N, group_size) ? workspace_for(plan_m1(K, N, group_size, sms))
+                                                     : workspace_for(plan_decode(M, K, N, km, sms));
+    const size_t c = workspace_for(plan_decode(M, K, N, km, sms));
+    return a > b ? (a > c ? a : c) : (b > c ? b : c);
+  }
   if (use_m1(km, M, K, N, group_size)) {
     // a weight or scale view that is not 8 / 4-byte aligned runs the generic kernel,
     // and this query does not see the pointers: cover both plans
@@ -237,8 +254,8 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
   if (M == 0) return GRINQH_OK;
 
-  if (use_m1tc(km, M, K, N, group)) {
-    const M1TcPlan plan = plan_m1tc(K, N, sms);
+  if (use_m1tc(km, M, K, N, group) && m1tc_pointers_ok(w) && m1tc_plan_fits(plan_m1tc(K, N, max_bits / 2, sms))) {
+    const M1TcPlan plan = plan_m1tc(K, N, max_bits / 2, sms);
     const size_t need = workspace_for(plan);
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
@@ -253,6 +270,8 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     g.N = (int)N;
     g.tiles = plan.tiles;
     g.units_per_cta = plan.units_per_cta;
+    g.bslots = plan.bslots;
+    g.tma_min_rows = tc_tma_min_rows();
     for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
     GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
                                     &g.counters));

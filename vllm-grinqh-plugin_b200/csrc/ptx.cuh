@@ -74,10 +74,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Wait for the phase with the given parity to complete. Gives up (records it and
 // returns false) after kWaitNs, or at once when another wait already gave up, so a
 // stalled pipeline ends the kernel quickly instead of hanging the GPU.
+#ifndef GRINQH_WAIT_SLEEP_NS
+#define GRINQH_WAIT_SLEEP_NS 0
+#endif
 static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
+#if GRINQH_WAIT_SLEEP_NS > 0
+    __nanosleep(GRINQH_WAIT_SLEEP_NS);  // leave the issue slots to the warps that have work
+#endif
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u) return false;
@@ -103,6 +109,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
+}
+
+// Close the group of this thread's cp.async issued since the last commit; wait until
+// at most N of its groups are still in flight.
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Arrive on `bar` once all cp.async of this thread issued so far have landed
