@@ -18,10 +18,12 @@
 // words of two rows 8 apart (same columns, same scales), reads their
 // planes from shared memory, merges them into codes, multiplies by the group scale,
 // rounds once to the activation dtype -- the reference's dtype(w * s), bit for bit --
-// and stores the weight stage; thread 0 also loads each step's x tile. Warp 9 issues
-// the MMAs (per 16-deep K slice, one tcgen05.mma kind::f16 per 128-column block,
-// N = Mp) from one thread into TMEM; tcgen05.commit frees the stage. The converters
-// never wait on global memory: the plane ring hides its latency.
+// and stores the weight stage. Warp 9 issues the MMAs (per 16-deep K slice, one
+// tcgen05.mma kind::f16 per 128-column block, N = Mp) from one thread into TMEM;
+// tcgen05.commit frees the stage, and a second lane of warp 9 then loads the x tile
+// of the step that reuses it (the x loads stay off the plane loader's TMA queue and
+// out of the converters' loop). The converters never wait on global memory: the
+// plane ring hides its latency.
 //
 // K is split over the CTAs of a thread-block cluster (and over several clusters for
 // long K). Each CTA stages its fp32 partial tile in shared memory; rank r of the
@@ -185,21 +187,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&empty[s]);
       }
       mma_commit(acc_full);
+    } else if (lane == 1) {
+      // activations: x of step i into stage i % SW as soon as the MMAs of step i - SW
+      // have released it, so the load is in flight well before the MMAs need it
+      prefetch_tmap(&tmap_x);
+      const uint32_t xbytes = (uint32_t)mp * BK * 2;
+      for (int i = 0; i < nq; ++i) {
+        const int s = i % SW;
+        if (i >= SW) mbar_wait(&empty[s], ((i / SW) - 1) & 1);
+        mbar_arrive_expect_tx(&x_full[s], xbytes);
+        tma_load_2d(sX + s * kStageX, &tmap_x, (q0 + i) * BK, 0, &x_full[s]);
+      }
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ converters
     // a warp covers 8 rows x 4 word pairs, twice: in every shared-memory access the 8
     // lanes of a phase are 8 different rows, which the 128-byte swizzle spreads over
     // all banks
-    const int ct = threadIdx.x;                      // 0..255
     const int rr = 16 * (warp & 1) + (lane & 7);     // rows rr and rr + 8 of each step
     const int jp = 4 * (warp >> 1) + (lane >> 3);    // this thread's words: 2 jp, 2 jp + 1
     const int jw = jt0 + 2 * jp;
     const bool jvalid = jw < n16;      // n16 is even: both words are valid or neither
     const int spg = a.group / BK;      // K steps per scale group
-    const bool x_issuer = ct == 0;
-    if (x_issuer) prefetch_tmap(&tmap_x);
-    const uint32_t xbytes = (uint32_t)mp * BK * 2;
     // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
     // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u
     constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
@@ -250,10 +260,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((g + 1) * spg < q0 + nq) load_scales(g + 1);
       }
       if (i >= SW) mbar_wait(&empty[s], ((i / SW) - 1) & 1);
-      if (x_issuer) {
-        mbar_arrive_expect_tx(&x_full[s], xbytes);
-        tma_load_2d(sX + s * kStageX, &tmap_x, q * BK, 0, &x_full[s]);
-      }
       mbar_wait(&p_full[ps], (i / SP) & 1);
       // plane words of the two words of rows rr, rr + 8 (the planes are 128-byte
       // swizzled by the TMA: 16-byte chunk c of row r sits at chunk c ^ (r & 7))
