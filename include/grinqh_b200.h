@@ -12,6 +12,7 @@
  *   grinqh_pack_words        <- grinqh/utils.py:125-146  pack_triton / _pack_kernel_uint32 (:100-122)
  *   grinqh_pack_codes        <- grinqh/grinqh.py:202-211 process_weights_after_loading
  *                               (grinqh_input_preshuffle utils.py:17-22, << (8-b), pack_triton)
+ *   grinqh_unpack_checkpoint <- grinqh/grinqh.py:154-168 weight loader (unpack_from_int32 + narrow + copy)
  *   grinqh_unpack            <- grinqh/utils.py:149-177  unpack_pyt, :209-223 unpack_triton
  *   grinqh_grade             <- grinqh/kernel.py:100-116 threshold masks of the graded GEMV
  *   grinqh_gemm_or_gemv      <- grinqh/kernel.py:646-710 torch.ops.grinqh.gemm_or_gemv
@@ -96,6 +97,18 @@ int grinqh_pack_words(const uint32_t *words_dev, uint32_t *out_dev, int64_t K, i
  * out_dev [K, (b/2)*N/16] uint32. Replaces grinqh/grinqh.py:202-211, bit-exact. */
 int grinqh_pack_codes(const int8_t *codes_dev, int64_t ld, uint32_t *out_dev, int64_t K, int64_t N,
                       int max_bits, grinqh_stream_t stream);
+
+/* Checkpoint codes -> this rank's staging codes in one pass (load time).
+ * src_dev: the compressed-tensors pack-quantized weight of one shard, rows = output
+ * features, src_ld int32 words per row, 32/b offset-binary fields per word LSB first
+ * along K (b = 2, 4, 8); for b = 6 the int8 codes themselves, src_ld bytes per row.
+ * Writes dst_dev[k * ld + n] = code(row r0 + n, column k0 + k) as int8 for n < rows,
+ * k < k_local; k0 a multiple of 32/b. Replaces unpack_from_int32 + the narrowing +
+ * the transposed copy of grinqh/grinqh.py:154-168 (compressed_tensors
+ * compressors/pack_quantized/helpers.py unpack_from_int32), bit-exact. */
+int grinqh_unpack_checkpoint(const void *src_dev, int64_t src_ld, int max_bits, int64_t r0, int64_t rows,
+                             int64_t k0, int64_t k_local, int8_t *dst_dev, int64_t ld,
+                             grinqh_stream_t stream);
 
 /* Inverse of grinqh_pack_words: out_dev [K, N] uint8, byte = shifted_code >> (8-b)
  * (unsigned, preshuffled column order), exactly unpack_pyt (grinqh/utils.py:149-177). */

@@ -109,6 +109,63 @@ __global__ void grade_kernel(const T* __restrict__ x, int64_t M, int64_t K, floa
   if (uni) uni[k] = (uint8_t)u;
 }
 
+
+// Checkpoint -> staging codes (load time): the compressed-tensors pack-quantized
+// weight (rows = output features, packed_dim 1: 32/b offset-binary fields per int32,
+// LSB first along K; compressed_tensors .../pack_quantized/helpers.py unpack_from_int32)
+// narrowed to rows [r0, r0 + rows) and columns [k0, k0 + k_local), transposed into
+// dst[k * ld + n] as signed int8 codes. PF = fields per word; PF = 1 reads int8 codes
+// directly (b = 6 checkpoints store the codes unpacked, grinqh/grinqh.py:131-132).
+// A 64 x 64 tile goes through shared memory so that both the reads (along K) and the
+// writes (along N) are contiguous.
+constexpr int kCkTile = 64;
+
+template <int B, int PF>
+__global__ void __launch_bounds__(256) unpack_checkpoint_kernel(const void* __restrict__ src, int64_t src_ld,
+                                                               int64_t r0, int64_t rows, int64_t k0,
+                                                               int64_t k_local, int8_t* __restrict__ dst,
+                                                               int64_t ld, bool vec_store) {
+  __shared__ int8_t tile[kCkTile][kCkTile + 4];  // [k][n]
+  const int64_t nb = blockIdx.x * (int64_t)kCkTile, kb = blockIdx.y * (int64_t)kCkTile;
+  constexpr int kUnits = PF > 1 ? kCkTile / PF : kCkTile / 4;  // loads per tile row
+  for (int t = threadIdx.x; t < kCkTile * kUnits; t += blockDim.x) {
+    const int rr = t / kUnits, u = t % kUnits;
+    const int64_t n = nb + rr;
+    if (n >= rows) continue;
+    if (PF > 1) {
+      const int64_t kk0 = kb + (int64_t)u * PF;  // first column of this word within the rank slice
+      if (kk0 >= k_local) continue;
+      const uint32_t w =
+          static_cast<const uint32_t*>(src)[(r0 + n) * src_ld + (k0 + kk0) / PF];  // k0 % PF == 0
+#pragma unroll
+      for (int i = 0; i < PF; ++i)
+        if (kk0 + i < k_local)
+          tile[u * PF + i][rr] = (int8_t)((int)((w >> (B * i)) & ((1u << B) - 1u)) - (1 << (B - 1)));
+    } else {
+      const int8_t* row = static_cast<const int8_t*>(src) + (r0 + n) * src_ld + k0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t kk = kb + 4 * u + i;
+        if (kk < k_local) tile[4 * u + i][rr] = row[kk];
+      }
+    }
+  }
+  __syncthreads();
+  // 16 threads per k row, 4 consecutive n each
+  for (int t = threadIdx.x; t < kCkTile * (kCkTile / 4); t += blockDim.x) {
+    const int kk = t / (kCkTile / 4), q = t % (kCkTile / 4);
+    const int64_t k = kb + kk, n = nb + 4 * q;
+    if (k >= k_local || n >= rows) continue;
+    int8_t* o = dst + k * ld + n;
+    if (vec_store && n + 4 <= rows) {
+      *reinterpret_cast<char4*>(o) =
+          make_char4(tile[kk][4 * q], tile[kk][4 * q + 1], tile[kk][4 * q + 2], tile[kk][4 * q + 3]);
+    } else {
+      for (int i = 0; i < 4 && n + i < rows; ++i) o[i] = tile[kk][4 * q + i];
+    }
+  }
+}
+
 }  // namespace
 }  // namespace grinqh
 
@@ -170,6 +227,30 @@ extern "C" int grinqh_unpack(const uint32_t* packed, uint8_t* out, int64_t K, in
     default: unpack_kernel<4><<<grid, block, 0, stream>>>(packed, o, K, N); break;
   }
   return check_launch("unpack");
+}
+
+extern "C" int grinqh_unpack_checkpoint(const void* src, int64_t src_ld, int max_bits, int64_t r0, int64_t rows,
+                                        int64_t k0, int64_t k_local, int8_t* dst, int64_t ld,
+                                        grinqh_stream_t stream) {
+  GRINQH_RETURN_IF(check_device());
+  if (!valid_bits(max_bits)) return set_error(GRINQH_ERR_UNSUPPORTED, "max_bits must be 2, 4, 6 or 8 (got %d)", max_bits);
+  GRINQH_REQUIRE(src && dst, "null pointer");
+  GRINQH_REQUIRE(r0 >= 0 && rows >= 0 && k0 >= 0 && k_local >= 0 && ld >= rows, "invalid slice");
+  const int pf = max_bits == 6 ? 1 : 32 / max_bits;
+  GRINQH_REQUIRE(k0 % (pf > 1 ? pf : 1) == 0, "k0 (%lld) must be a multiple of %d", (long long)k0, pf);
+  GRINQH_REQUIRE(pf == 1 ? src_ld >= k0 + k_local : src_ld * pf >= k0 + k_local,
+                 "source row of %lld elements is shorter than k0 + k_local", (long long)src_ld);
+  if (rows == 0 || k_local == 0) return GRINQH_OK;
+  const bool vec = aligned(dst, 4) && ld % 4 == 0;
+  const dim3 grid((unsigned)((rows + kCkTile - 1) / kCkTile), (unsigned)((k_local + kCkTile - 1) / kCkTile));
+  GRINQH_REQUIRE(grid.y <= 65535, "k_local too large");
+  switch (max_bits) {
+    case 2: unpack_checkpoint_kernel<2, 16><<<grid, 256, 0, stream>>>(src, src_ld, r0, rows, k0, k_local, dst, ld, vec); break;
+    case 4: unpack_checkpoint_kernel<4, 8><<<grid, 256, 0, stream>>>(src, src_ld, r0, rows, k0, k_local, dst, ld, vec); break;
+    case 6: unpack_checkpoint_kernel<8, 1><<<grid, 256, 0, stream>>>(src, src_ld, r0, rows, k0, k_local, dst, ld, vec); break;
+    default: unpack_checkpoint_kernel<8, 4><<<grid, 256, 0, stream>>>(src, src_ld, r0, rows, k0, k_local, dst, ld, vec); break;
+  }
+  return check_launch("unpack_checkpoint");
 }
 
 extern "C" int grinqh_grade(const void* x, int dtype, int64_t M, int64_t K, const float* thresholds,

@@ -188,6 +188,28 @@ at::Tensor pack_codes(const at::Tensor& codes, int64_t max_bits) {
   return out;
 }
 
+// checkpoint -> staging codes (grinqh/grinqh.py:154-168): src is the shard's
+// compressed-tensors int32 weight [rows_total, words] (or int8 codes for b = 6);
+// writes dst[:, n_off : n_off + rows] (int8 [K_local, N_local], any row stride) with
+// the codes of source rows [row0, row0 + rows) and columns [k0, k0 + dst.size(0))
+void unpack_checkpoint(const at::Tensor& src, int64_t max_bits, int64_t row0, int64_t rows, int64_t k0,
+                       const at::Tensor& dst, int64_t n_off) {
+  check_cuda(src, "src");
+  check_cuda(dst, "dst");
+  TORCH_CHECK(src.dim() == 2 && dst.dim() == 2, "GRINQH unpack_checkpoint: expects 2-D tensors");
+  TORCH_CHECK(max_bits == 6 ? src.scalar_type() == at::kChar : src.scalar_type() == at::kInt,
+              "GRINQH unpack_checkpoint: src must be int32 (int8 for max_bits 6)");
+  TORCH_CHECK(dst.scalar_type() == at::kChar && dst.stride(1) == 1, "GRINQH unpack_checkpoint: dst must be int8 with unit column stride");
+  TORCH_CHECK(src.device() == dst.device(), "GRINQH unpack_checkpoint: src and dst on different devices");
+  TORCH_CHECK(row0 >= 0 && rows >= 0 && row0 + rows <= src.size(0), "GRINQH unpack_checkpoint: row range out of bounds");
+  TORCH_CHECK(n_off >= 0 && n_off + rows <= dst.size(1), "GRINQH unpack_checkpoint: column range out of bounds");
+  const at::Tensor s = src.contiguous();
+  const c10::cuda::CUDAGuard guard(s.device());
+  check_ok(grinqh_unpack_checkpoint(s.data_ptr(), s.size(1), (int)max_bits, row0, rows, k0, dst.size(0),
+                                    dst.data_ptr<int8_t>() + n_off, dst.stride(0), cur_stream(s)),
+           "unpack_checkpoint");
+}
+
 // unpack (grinqh/utils.py:149-177): [K, (b/2)*N/16] -> [K, N] uint8 (shifted code >> (8-b))
 at::Tensor unpack(const at::Tensor& packed, int64_t max_bits, int64_t original_n) {
   check_cuda(packed, "packed");
@@ -231,6 +253,7 @@ TORCH_LIBRARY(grinqh, m) {
   m.def("pack(Tensor words, int max_bits) -> Tensor");
   m.def("pack_codes(Tensor codes, int max_bits) -> Tensor");
   m.def("unpack(Tensor packed, int max_bits, int original_n) -> Tensor");
+  m.def("unpack_checkpoint(Tensor src, int max_bits, int row0, int rows, int k0, Tensor(a!) dst, int n_off) -> ()");
   m.def("grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor)");
 }
 
@@ -240,5 +263,6 @@ TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
   m.impl("pack", &pack);
   m.impl("pack_codes", &pack_codes);
   m.impl("unpack", &unpack);
+  m.impl("unpack_checkpoint", &unpack_checkpoint);
   m.impl("grade", &grade);
 }

@@ -30,6 +30,7 @@ SIGNATURES = {
     "grinqh_take_error_flags": (_int, [_ptr]),
     "grinqh_pack_words": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_pack_codes": (_int, [_ptr, _i64, _ptr, _i64, _i64, _int, _ptr]),
+    "grinqh_unpack_checkpoint": (_int, [_ptr, _i64, _int, _i64, _i64, _i64, _i64, _ptr, _i64, _ptr]),
     "grinqh_unpack": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_grade": (_int, [_ptr, _int, _i64, _i64, _fptr, _int, _ptr, _ptr, _ptr]),
     "grinqh_workspace_size": (_size, [_i64, _i64, _i64, _int, _int, _int]),

@@ -30,7 +30,7 @@ from vllm.model_executor.layers.quantization.utils.layer_utils import replace_pa
 from vllm.model_executor.utils import set_weight_attrs
 
 from .kernel import grinqh_gemm_or_gemv  # noqa: F401  (registers torch.ops.grinqh)
-from .utils import pack_codes
+from .utils import pack_codes, unpack_checkpoint
 
 logger = init_logger("vllm.grinqh")
 
@@ -56,6 +56,17 @@ def shard_rank_for(layer, shard_id, tp_rank: int) -> int:
     if shard_id in ("k", "v"):
         return tp_rank // int(getattr(layer, "num_kv_head_replicas", 1) or 1)
     return tp_rank
+
+
+def checkpoint_row0(rows_total: int, out_rows: int, out_rank: int) -> int:
+    """First checkpoint row of this rank's slice (the row narrowing of
+    :func:`narrow_checkpoint`)."""
+    if rows_total == out_rows:
+        return 0
+    if rows_total < (out_rank + 1) * out_rows:
+        raise ValueError(f"GRINQH: checkpoint shard has {rows_total} rows, rank slice {out_rank} of "
+                         f"{out_rows} does not fit")
+    return out_rank * out_rows
 
 
 def narrow_checkpoint(t: torch.Tensor, out_rows: int, out_rank: int, in_cols: Optional[int], in_rank: int):
@@ -178,6 +189,16 @@ class GRINQHLinearMethod(LinearMethodBase):
                 # (N, K/g) in the checkpoint -> this rank's (K_local/g, N slice)
                 s = narrow_checkpoint(loaded_weight, out_rows, out_rank, k_local // group, in_rank)
                 param.data[:, n_off:n_off + out_rows].copy_(s.to(param.device).T)
+                return
+            if param.data.is_cuda:
+                # one kernel: unpack + rank narrowing + transposed copy into the staging codes
+                src = loaded_weight.to(param.device)
+                row0 = checkpoint_row0(src.shape[0], out_rows, out_rank)
+                k0 = 0 if input_size == k_local else in_rank * k_local
+                if k0 + k_local > input_size:
+                    raise ValueError(f"GRINQH: checkpoint has {input_size} input columns, rank slice {in_rank} of "
+                                     f"{k_local} does not fit")
+                unpack_checkpoint(src, num_bits, row0, out_rows, k0, param.data.view(torch.int8), n_off)
                 return
             w = loaded_weight.to(param.device)
             if num_bits != 6:  # b=6 checkpoints store int8 codes (grinqh.py:151-153)

@@ -49,6 +49,11 @@ def _fake_pack_codes(codes, max_bits):
     return codes.new_empty((codes.shape[0], (max_bits // 2) * (codes.shape[1] // 16)), dtype=torch.uint32)
 
 
+@torch.library.register_fake("grinqh::unpack_checkpoint")
+def _fake_unpack_checkpoint(src, max_bits, row0, rows, k0, dst, n_off):
+    return None
+
+
 @torch.library.register_fake("grinqh::unpack")
 def _fake_unpack(packed, max_bits, original_n):
     return packed.new_empty((packed.shape[0], original_n * 4), dtype=torch.uint8)

@@ -58,6 +58,16 @@ def pack_codes(codes: torch.Tensor, max_bits: int = 8) -> torch.Tensor:
     return torch.ops.grinqh.pack_codes(codes, max_bits)
 
 
+def unpack_checkpoint(src: torch.Tensor, max_bits: int, row0: int, rows: int, k0: int, dst: torch.Tensor,
+                      n_off: int) -> None:
+    """One load-time kernel for a checkpoint shard (grinqh.py:154-168): unpack the
+    compressed-tensors int32 weight ``src`` (rows = output features; int8 codes for
+    b = 6), narrow it to rows ``[row0, row0 + rows)`` and columns
+    ``[k0, k0 + dst.shape[0])``, and write the int8 codes transposed into
+    ``dst[:, n_off:n_off + rows]``."""
+    torch.ops.grinqh.unpack_checkpoint(src, max_bits, row0, rows, k0, dst, n_off)
+
+
 def _bit_level(bit_level) -> int:
     return int(bit_level.value if isinstance(bit_level, BitLevel) else bit_level)
 
