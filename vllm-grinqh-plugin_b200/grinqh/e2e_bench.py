@@ -2,6 +2,7 @@
 
     python -m grinqh.e2e_bench [--tp N] [--batch 64] [--prompt 512] [--gen 256]
                                [--arch 8b|70b] [--max-bits 8] [--enforce-eager]
+                               [--checkpoint DIR]
 
 Builds a local model directory with the Llama-3 architecture's config.json (8B:
 hidden 4096, FFN 14336, 32 layers, 32 / 8 heads; 70B: 8192, 28672, 80, 64 / 8;
@@ -13,6 +14,10 @@ the allocation holds, the bf16 scales are uniform in [-1e-3, 1e-3]); every
 packs the planes on the GPU; apply calls torch.ops.grinqh.gemm_or_gemv). Prompts are
 uniform random token ids, generation is greedy with ``ignore_eos`` so every sequence
 produces exactly ``--gen`` tokens.
+
+With ``--checkpoint DIR`` it runs a checkpoint written by ``python -m grinqh.quantize``
+(real codes, scales and calibrated thresholds from its config) instead of the random
+model.
 
 Reported (one JSON line): output tokens / second over the whole generate call, the
 decode-only rate (generate time minus a prefill-only call with one output token),
@@ -96,20 +101,26 @@ def main() -> None:
     ap.add_argument("--max-bits", type=int, default=8)
     ap.add_argument("--gpu-memory-utilization", type=float, default=0.6)
     ap.add_argument("--enforce-eager", action="store_true")
+    ap.add_argument("--checkpoint", default=None, help="a GRINQH checkpoint directory (grinqh.quantize)")
     args = ap.parse_args()
 
     root = tempfile.mkdtemp(prefix="grinqh_e2e_")
-    model_dir = write_model(root, args.arch, args.max_bits, args.layers)
+    if args.checkpoint:
+        model_dir, load_format = args.checkpoint, "auto"
+        with open(os.path.join(model_dir, "config.json")) as f:
+            vocab = json.load(f)["vocab_size"]
+    else:
+        model_dir, load_format, vocab = write_model(root, args.arch, args.max_bits, args.layers), "dummy", 128256
     expose_plugin(root)
 
     import numpy as np
     from vllm import LLM, SamplingParams
 
-    llm = LLM(model=model_dir, quantization="grinqh", load_format="dummy", tensor_parallel_size=args.tp,
+    llm = LLM(model=model_dir, quantization="grinqh", load_format=load_format, tensor_parallel_size=args.tp,
               skip_tokenizer_init=True, dtype="bfloat16", max_model_len=args.prompt + args.gen + 16,
               gpu_memory_utilization=args.gpu_memory_utilization, enforce_eager=args.enforce_eager, seed=0)
     rng = np.random.default_rng(0)
-    prompts = [{"prompt_token_ids": rng.integers(0, 128256, args.prompt).tolist()} for _ in range(args.batch)]
+    prompts = [{"prompt_token_ids": rng.integers(0, vocab, args.prompt).tolist()} for _ in range(args.batch)]
     gen = SamplingParams(max_tokens=args.gen, min_tokens=args.gen, ignore_eos=True, temperature=0.0,
                          detokenize=False)
     one = SamplingParams(max_tokens=1, ignore_eos=True, temperature=0.0, detokenize=False)
@@ -125,7 +136,8 @@ def main() -> None:
     decode_tokens = n_out - args.batch
     line = {
         "metric": "decode tok/s, Llama-3 GRINQH in vLLM (random weights)",
-        "arch": args.arch, "layers": args.layers or ARCH[args.arch]["num_hidden_layers"], "tp": args.tp,
+        "arch": args.checkpoint or args.arch, "layers": args.layers or ARCH[args.arch]["num_hidden_layers"],
+        "tp": args.tp,
         "batch": args.batch, "prompt": args.prompt, "gen": args.gen, "max_bits": args.max_bits,
         "output_tokens": n_out, "generate_s": round(t_all, 3), "prefill_s": round(t_prefill, 3),
         "output_tok_per_s": round(n_out / t_all, 1),
