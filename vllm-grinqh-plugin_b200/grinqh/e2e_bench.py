@@ -135,7 +135,7 @@ def main() -> None:
     n_out = sum(len(o.outputs[0].token_ids) for o in outs)
     decode_tokens = n_out - args.batch
     line = {
-        "metric": "decode tok/s, Llama-3 GRINQH in vLLM (random weights)",
+        "metric": "decode tok/s, Llama GRINQH in vLLM (" + ("checkpoint" if args.checkpoint else "random weights") + ")",
         "arch": args.checkpoint or args.arch, "layers": args.layers or ARCH[args.arch]["num_hidden_layers"],
         "tp": args.tp,
         "batch": args.batch, "prompt": args.prompt, "gen": args.gen, "max_bits": args.max_bits,
