@@ -1,6 +1,8 @@
 // C ABI entry points of the quantized linear and shared status plumbing.
 #include <mutex>
 
+#include <cstring>
+
 #include "common.cuh"
 
 #include <stdlib.h>
@@ -384,6 +386,101 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     GRINQH_RETURN_IF(bind_workspace(workspace, plan.partial_bytes, plan.counter_bytes, zeroed, stream, &a.partial,
                                     &a.counters));
   return launch_decode(a, plan, km, dtype, max_bits / 2, stream);
+}
+
+// ---------------------------------------------------------------- fused all-reduce
+extern "C" size_t grinqh_allreduce_buffer_bytes(int world, int64_t max_n) {
+  if (world < 1 || world > kArMaxRanks || max_n <= 0) return 0;
+  return m1_allreduce_buffer_bytes(world, max_n);
+}
+
+extern "C" int grinqh_allreduce_buffer_alloc(size_t bytes, void** buf) {
+  GRINQH_RETURN_IF(check_device());
+  GRINQH_REQUIRE(buf && bytes >= kArParts, "null pointer or buffer too small");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);  // epoch, ticket and flags start at 0
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_error(GRINQH_ERR_CUDA, "clearing the peer buffer: %s", cudaGetErrorString(e));
+  }
+  *buf = p;
+  return GRINQH_OK;
+}
+
+extern "C" int grinqh_allreduce_buffer_free(void* buf) {
+  if (!buf) return GRINQH_OK;
+  const cudaError_t e = cudaFree(buf);
+  return e == cudaSuccess ? GRINQH_OK : set_error(GRINQH_ERR_CUDA, "cudaFree: %s", cudaGetErrorString(e));
+}
+
+extern "C" int grinqh_ipc_get_handle(const void* buf, unsigned char* handle64) {
+  GRINQH_REQUIRE(buf && handle64, "null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(buf));
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle64, &h, 64);
+  return GRINQH_OK;
+}
+
+extern "C" int grinqh_ipc_open_handle(const unsigned char* handle64, void** buf) {
+  GRINQH_REQUIRE(handle64 && buf, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, 64);
+  const cudaError_t e = cudaIpcOpenMemHandle(buf, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  return GRINQH_OK;
+}
+
+extern "C" int grinqh_ipc_close_handle(void* buf) {
+  if (!buf) return GRINQH_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(buf);
+  return e == cudaSuccess ? GRINQH_OK : set_error(GRINQH_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+}
+
+extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const uint32_t* w, const void* s,
+                                     const void* bias, int max_bits, int group, int64_t N, const float* thresholds,
+                                     void* y, void* workspace, size_t workspace_bytes, int rank, int world,
+                                     void* const* buffers, int64_t n_cap, int mode, grinqh_stream_t stream) {
+  int dev = 0, sms = 0;
+  GRINQH_RETURN_IF(device_info(&dev, &sms));
+  GRINQH_RETURN_IF(validate(x, dtype, 1, K, w, s, max_bits, group, N, y));
+  GRINQH_REQUIRE(thresholds, "thresholds required");
+  GRINQH_REQUIRE(world >= 1 && world <= kArMaxRanks && rank >= 0 && rank < world, "rank %d of %d (at most %d ranks)",
+                 rank, world, kArMaxRanks);
+  GRINQH_REQUIRE(buffers && N <= n_cap, "peer buffers hold %lld columns, N is %lld", (long long)n_cap, (long long)N);
+  for (int r = 0; r < world; ++r) GRINQH_REQUIRE(buffers[r] && aligned(buffers[r], 256), "peer buffer %d", r);
+  if (!m1_supported(1, K, N, group) || !m1_pointers_ok(w, s))
+    return set_error(GRINQH_ERR_UNSUPPORTED, "fused all-reduce: shape or alignment not supported by the GEMV");
+  const bool zeroed = (mode & GRINQH_WORKSPACE_ZEROED) != 0;
+  const M1Plan plan = plan_m1(K, N, group, sms);
+  const size_t need = workspace_for(plan);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
+  M1Args g{};
+  g.x = x;
+  g.w = w;
+  g.s = s;
+  g.bias = bias;
+  g.y = y;
+  g.K = (int)K;
+  g.N = (int)N;
+  g.group = group;
+  g.rows_per_warp = plan.rows_per_warp;
+  g.rows_per_cta = plan.rows_per_cta;
+  for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
+  g.ar.rank = rank;
+  g.ar.world = world;
+  g.ar.n_cap = (int)n_cap;
+  for (int r = 0; r < world; ++r) g.ar.buf[r] = static_cast<unsigned char*>(buffers[r]);
+  if (need > 0)
+    GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
+                                    &g.counters));
+  return launch_m1(g, plan, dtype, max_bits / 2, stream, true);
 }
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {

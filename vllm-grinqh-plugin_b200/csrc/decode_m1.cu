@@ -191,7 +191,73 @@ __device__ __forceinline__ void warp_chunk(const M1Args& a, int tile, int kb, in
   flush();
 }
 
-template <int NZ, typename T>
+// ---------------------------------------------------------------- fused all-reduce
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Runs in every finalizing CTA (one per column slice) after it has written its
+// slice's sums into every rank's buffer. The last of them on this rank (ticket):
+// announces the epoch to every rank, waits (bounded) until every rank has announced
+// it here, then adds the ranks' partials in rank order -- the same order on every
+// rank, so all ranks get the same bits -- adds the bias and writes y.
+template <typename T>
+__device__ void allreduce_tail(const M1Args& a, unsigned epoch, int* s_flag) {
+  const M1AllReduce& ar = a.ar;
+  unsigned* ctrl = reinterpret_cast<unsigned*>(ar.buf[ar.rank]);
+  __syncthreads();  // this CTA's partial stores are issued
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // ... and visible to every rank before the ticket
+    *s_flag = atomicAdd(ctrl + 1, 1u) == gridDim.x - 1u;  // one finalizing CTA per slice
+  }
+  __syncthreads();
+  if (!*s_flag) return;
+  __threadfence_system();
+  if (threadIdx.x < (unsigned)ar.world) {
+    const int r = threadIdx.x;
+    st_release_sys(reinterpret_cast<unsigned*>(ar.buf[r] + kArFlags) + ar.rank, epoch);
+    const unsigned* mine = reinterpret_cast<const unsigned*>(ar.buf[ar.rank] + kArFlags) + r;
+    if (ld_acquire_sys(mine) != epoch) {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 1;; ++it) {
+        __nanosleep(64);
+        if (ld_acquire_sys(mine) == epoch) break;
+        if ((it & 255u) == 0) {
+          // after any wait of this library gave up, give up at once (the output is
+          // invalid anyway and the host sees the count); else after kWaitNs
+          if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u) break;
+          if (globaltimer_ns() - t0 > kWaitNs) {  // a rank never arrived
+            atomicAdd(&g_wait_timeouts, 1u);
+            break;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const float* parts = reinterpret_cast<const float*>(ar.buf[ar.rank] + kArParts) +
+                       (size_t)(epoch & 1u) * ar.world * ar.n_cap;
+  T* y = static_cast<T*>(a.y);
+  const T* bias = static_cast<const T*>(a.bias);
+  for (int n = threadIdx.x; n < a.N; n += blockDim.x) {
+    float v = 0.f;
+    for (int r = 0; r < ar.world; ++r) v += __ldcv(parts + (size_t)r * ar.n_cap + n);
+    T out = Act<T>::from_f(v);
+    if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[n]));
+    y[n] = out;
+  }
+  if (threadIdx.x == 0) {
+    ctrl[1] = 0u;      // ticket ready for the next launch
+    ctrl[0] = epoch;   // read by the next launch after griddepcontrol.wait
+  }
+}
+
+template <int NZ, typename T, bool kAR>
 __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   extern __shared__ __align__(16) unsigned char smem[];
   RowMeta* rows = reinterpret_cast<RowMeta*>(smem);  // staged rows of the CTA
@@ -225,6 +291,8 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     }
   }
   wait_prior_grid();  // x and the outputs belong to the stream order from here on
+  // epoch of this launch (fused all-reduce): one more than the last completed one
+  const unsigned ar_epoch = kAR ? *reinterpret_cast<volatile unsigned*>(a.ar.buf[a.ar.rank]) + 1u : 0u;
   warp_chunk<NZ, T>(a, tile, rb, re, rows + (rb - k0), wacc);
   allow_dependent_grid();
 
@@ -261,6 +329,11 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     const int jx = tile * kSliceW + jj;
     if (jx >= n16) return;
     const int nn = c * n16 + jx;
+    if constexpr (kAR) {  // this rank's partial, into every rank's buffer (NVLink stores)
+      const size_t off = ((size_t)(ar_epoch & 1u) * a.ar.world + a.ar.rank) * a.ar.n_cap + nn;
+      for (int r = 0; r < a.ar.world; ++r) __stcg(reinterpret_cast<float*>(a.ar.buf[r] + kArParts) + off, v);
+      return;
+    }
     T out = Act<T>::from_f(v);
     if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[nn]));
     y[nn] = out;
@@ -269,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   if (nclu == 1) {
 #pragma unroll
     for (int h = 0; h < kSliceN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
+    if constexpr (kAR) allreduce_tail<T>(a, ar_epoch, &s_last);
     return;
   }
   const int clu = split / csize;
@@ -296,11 +370,12 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     store_y(col, v);
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
+  if constexpr (kAR) allreduce_tail<T>(a, ar_epoch, &s_last);
 }
 
-template <int NZ, typename T>
+template <int NZ, typename T, bool kAR>
 int launch_t(const M1Args& a, const M1Plan& p, cudaStream_t st) {
-  auto kern = m1_kernel<NZ, T>;
+  auto kern = m1_kernel<NZ, T, kAR>;
   const size_t smem = p.smem_bytes;
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -362,21 +437,26 @@ M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
   return p;
 }
 
-int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st) {
+template <bool kAR>
+int launch_m1_t(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st) {
   if (dtype == GRINQH_BF16) {
     switch (nz) {
-      case 1: return launch_t<1, __nv_bfloat16>(a, p, st);
-      case 2: return launch_t<2, __nv_bfloat16>(a, p, st);
-      case 3: return launch_t<3, __nv_bfloat16>(a, p, st);
-      default: return launch_t<4, __nv_bfloat16>(a, p, st);
+      case 1: return launch_t<1, __nv_bfloat16, kAR>(a, p, st);
+      case 2: return launch_t<2, __nv_bfloat16, kAR>(a, p, st);
+      case 3: return launch_t<3, __nv_bfloat16, kAR>(a, p, st);
+      default: return launch_t<4, __nv_bfloat16, kAR>(a, p, st);
     }
   }
   switch (nz) {
-    case 1: return launch_t<1, __half>(a, p, st);
-    case 2: return launch_t<2, __half>(a, p, st);
-    case 3: return launch_t<3, __half>(a, p, st);
-    default: return launch_t<4, __half>(a, p, st);
+    case 1: return launch_t<1, __half, kAR>(a, p, st);
+    case 2: return launch_t<2, __half, kAR>(a, p, st);
+    case 3: return launch_t<3, __half, kAR>(a, p, st);
+    default: return launch_t<4, __half, kAR>(a, p, st);
   }
+}
+
+int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st, bool allreduce) {
+  return allreduce ? launch_m1_t<true>(a, p, dtype, nz, st) : launch_m1_t<false>(a, p, dtype, nz, st);
 }
 
 }  // namespace grinqh

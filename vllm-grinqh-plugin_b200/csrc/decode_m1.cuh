@@ -7,6 +7,17 @@
 
 namespace grinqh {
 
+// Fused all-reduce over the tensor-parallel ranks' peer buffers (grinqh_gemv_allreduce).
+// Buffer of a rank: [0] epoch of its last completed launch, [1] launch ticket; at
+// kArFlags the epoch each rank last published into it; at kArParts the partial sums
+// [2 (epoch parity)][world][n_cap] fp32 written by every rank.
+constexpr int kArMaxRanks = 8;
+constexpr size_t kArFlags = 256, kArParts = 1024;
+struct M1AllReduce {
+  unsigned char* buf[kArMaxRanks];  // every rank's buffer as mapped in this process
+  int rank, world, n_cap;
+};
+
 struct M1Args {
   const void* x;        // [K] dtype
   const uint32_t* w;    // [K, nz*N/16] packed planes
@@ -17,6 +28,7 @@ struct M1Args {
   unsigned* counters;   // [tiles] tickets; zero before the first launch, left zero
   int K, N, group, rows_per_warp, rows_per_cta;
   float t[4];
+  M1AllReduce ar;       // used by the fused all-reduce launch only
 };
 
 struct M1Plan {
@@ -35,6 +47,9 @@ inline bool m1_pointers_ok(const void* w, const void* s) {
   return (reinterpret_cast<uintptr_t>(w) % 8) == 0 && (reinterpret_cast<uintptr_t>(s) % 4) == 0;
 }
 M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
-int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st);
+int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st, bool allreduce = false);
+inline size_t m1_allreduce_buffer_bytes(int world, int64_t n_cap) {
+  return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(float);
+}
 
 }  // namespace grinqh

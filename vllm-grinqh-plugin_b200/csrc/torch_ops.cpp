@@ -141,6 +141,52 @@ at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, cons
   return y.view(out_shape);
 }
 
+// Row-parallel linear of one row with the tensor-parallel sum fused in (the C ABI's
+// grinqh_gemv_allreduce): buffers are every rank's peer buffer address as mapped in
+// this process, from grinqh.allreduce.PeerBuffers.
+at::Tensor gemv_allreduce(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                          const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
+                          int64_t original_n, at::ArrayRef<double> thresholds, int64_t rank, int64_t world,
+                          at::ArrayRef<int64_t> buffers, int64_t n_cap) {
+  check_cuda(x, "x");
+  check_cuda(weight_packed, "weight_packed");
+  check_cuda(weight_scale, "weight_scale");
+  const int dt = dtype_code(x, "x");
+  TORCH_CHECK(weight_scale.scalar_type() == x.scalar_type(), "GRINQH: weight_scale dtype != x dtype");
+  TORCH_CHECK(is_word32(weight_packed) && weight_packed.dim() == 2 && weight_scale.dim() == 2,
+              "GRINQH: weight_packed must be 2-D int32/uint32 and weight_scale 2-D");
+  const int64_t K = weight_packed.size(0), N = original_n * 4;
+  TORCH_CHECK(x.numel() == K, "GRINQH gemv_allreduce: x must hold exactly one row of K = ", K, " values");
+  TORCH_CHECK((int64_t)buffers.size() == world, "GRINQH gemv_allreduce: one buffer per rank");
+  if (bias) {
+    check_cuda(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == x.scalar_type() && bias->numel() == N, "GRINQH: bias must be [N] of x's dtype");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor xf = x.reshape({1, K}).contiguous();
+  const at::Tensor wp = weight_packed.contiguous();
+  const at::Tensor sc = weight_scale.contiguous();
+  const at::Tensor bc = bias ? bias->contiguous() : at::Tensor();
+  std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
+  out_shape.back() = N;
+  at::Tensor y = at::empty({1, N}, x.options());
+  const auto th = thresholds4(thresholds);
+  const size_t ws_bytes = grinqh_workspace_size(1, K, N, (int)max_bits, (int)group_size, GRINQH_MODE_AUTO);
+  const cudaStream_t stream = cur_stream(x);
+  at::Tensor ws;
+  bool zeroed = false;
+  if (ws_bytes) ws = stream_workspace(x, ws_bytes, stream, &zeroed);
+  std::vector<void*> bufs(buffers.size());
+  for (size_t r = 0; r < buffers.size(); ++r) bufs[r] = reinterpret_cast<void*>(buffers[r]);
+  check_ok(grinqh_gemv_allreduce(xf.data_ptr(), dt, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()), sc.data_ptr(),
+                                 bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N, th.data(),
+                                 y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr,
+                                 ws_bytes ? static_cast<size_t>(ws.numel()) : 0, (int)rank, (int)world, bufs.data(),
+                                 n_cap, zeroed ? GRINQH_WORKSPACE_ZEROED : 0, stream),
+           "gemv_allreduce");
+  return y.view(out_shape);
+}
+
 // torch.ops.grinqh.gemm_or_gemv -- grinqh/kernel.py:646-710. use_marlin is accepted
 // for schema compatibility and ignored (no Marlin path in this build).
 at::Tensor gemm_or_gemv(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
@@ -254,6 +300,8 @@ TORCH_LIBRARY(grinqh, m) {
   m.def("pack_codes(Tensor codes, int max_bits) -> Tensor");
   m.def("unpack(Tensor packed, int max_bits, int original_n) -> Tensor");
   m.def("unpack_checkpoint(Tensor src, int max_bits, int row0, int rows, int k0, Tensor(a!) dst, int n_off) -> ()");
+  m.def("gemv_allreduce(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
+        "int group_size, int original_n, float[] thresholds, int rank, int world, int[] buffers, int n_cap) -> Tensor");
   m.def("grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor)");
 }
 
@@ -264,5 +312,6 @@ TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
   m.impl("pack_codes", &pack_codes);
   m.impl("unpack", &unpack);
   m.impl("unpack_checkpoint", &unpack_checkpoint);
+  m.impl("gemv_allreduce", &gemv_allreduce);
   m.impl("grade", &grade);
 }

@@ -31,6 +31,14 @@ SIGNATURES = {
     "grinqh_pack_words": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_pack_codes": (_int, [_ptr, _i64, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_unpack_checkpoint": (_int, [_ptr, _i64, _int, _i64, _i64, _i64, _i64, _ptr, _i64, _ptr]),
+    "grinqh_allreduce_buffer_bytes": (ctypes.c_size_t, [_int, _i64]),
+    "grinqh_allreduce_buffer_alloc": (_int, [ctypes.c_size_t, _ptr]),
+    "grinqh_allreduce_buffer_free": (_int, [_ptr]),
+    "grinqh_ipc_get_handle": (_int, [_ptr, _ptr]),
+    "grinqh_ipc_open_handle": (_int, [_ptr, _ptr]),
+    "grinqh_ipc_close_handle": (_int, [_ptr]),
+    "grinqh_gemv_allreduce": (_int, [_ptr, _int, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _ptr, _ptr, _ptr,
+                                     ctypes.c_size_t, _int, _int, _ptr, _i64, _int, _ptr]),
     "grinqh_unpack": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_grade": (_int, [_ptr, _int, _i64, _i64, _fptr, _int, _ptr, _ptr, _ptr]),
     "grinqh_workspace_size": (_size, [_i64, _i64, _i64, _int, _int, _int]),

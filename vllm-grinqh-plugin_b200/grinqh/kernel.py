@@ -49,6 +49,12 @@ def _fake_pack_codes(codes, max_bits):
     return codes.new_empty((codes.shape[0], (max_bits // 2) * (codes.shape[1] // 16)), dtype=torch.uint32)
 
 
+@torch.library.register_fake("grinqh::gemv_allreduce")
+def _fake_gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds, rank,
+                         world, buffers, n_cap):
+    return x.new_empty((*x.shape[:-1], 4 * original_n))
+
+
 @torch.library.register_fake("grinqh::unpack_checkpoint")
 def _fake_unpack_checkpoint(src, max_bits, row0, rows, k0, dst, n_off):
     return None
