@@ -10,7 +10,7 @@ are ordered, and every rank makes the same calls in the same order).
 from __future__ import annotations
 
 import ctypes
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -86,3 +86,51 @@ def gemv_allreduce(x: torch.Tensor, weight_packed: torch.Tensor, weight_scale: t
     identical on every rank; ``bias`` (the full bias, on every rank) is added once."""
     return torch.ops.grinqh.gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n,
                                            list(thresholds), peers.rank, peers.world, peers.buffers, peers.n_cap)
+
+
+# ----------------------------------------------------------------------------- vLLM
+# One set of peer buffers per device, over vLLM's tensor-parallel group, created by
+# the first fused call (vLLM's profiling forward, before any CUDA-graph capture; every
+# rank runs that forward, so the collective setup lines up).
+_TP_PEERS: Dict[int, PeerBuffers] = {}
+
+
+def tp_peers(device: torch.device, n_cap: int) -> PeerBuffers:
+    from vllm.distributed import get_tp_group
+    key = torch.device(device).index or 0
+    p = _TP_PEERS.get(key)
+    if p is None or p.n_cap < n_cap:
+        p = PeerBuffers(get_tp_group().cpu_group, max(int(n_cap), 8192), device)
+        _TP_PEERS[key] = p
+    return p
+
+
+def fused_row_supported(x: torch.Tensor, weight_packed: torch.Tensor, original_n: int, group_size: int) -> bool:
+    """The fused kernel takes one row of x and the single-row GEMV's shapes."""
+    n = 4 * original_n
+    return (x.numel() == weight_packed.shape[0] and n % 32 == 0 and group_size % 4 == 0
+            and weight_packed.shape[0] % group_size == 0)
+
+
+@torch.library.custom_op("grinqh::row_parallel_linear", mutates_args=())
+def row_parallel_linear(x: torch.Tensor, weight_packed: torch.Tensor, weight_scale: torch.Tensor,
+                        bias: Optional[torch.Tensor], max_bits: int, group_size: int, original_n: int,
+                        thresholds: List[float]) -> torch.Tensor:
+    """A row-parallel linear with its tensor-parallel sum: ``bias`` is the full bias
+    (added once). One row: the fused kernel (GEMV + NVLink sum); more rows: the GEMM
+    followed by vLLM's all-reduce (RowParallelLinear.forward), bias on rank 0 only.
+    Opaque to the compiler, so the branch on the row count is taken at run time."""
+    from vllm.distributed import get_tensor_model_parallel_rank, tensor_model_parallel_all_reduce
+    if fused_row_supported(x, weight_packed, original_n, group_size):
+        peers = tp_peers(x.device, 4 * original_n)
+        return gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds,
+                              peers)
+    rank_bias = bias if get_tensor_model_parallel_rank() == 0 else None
+    y = torch.ops.grinqh.gemm_or_gemv(x, weight_packed, weight_scale, rank_bias, max_bits, group_size, original_n,
+                                      thresholds, False)
+    return tensor_model_parallel_all_reduce(y)
+
+
+@row_parallel_linear.register_fake
+def _(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds):
+    return x.new_empty((*x.shape[:-1], 4 * original_n))

@@ -29,6 +29,7 @@ from vllm.model_executor.layers.quantization.base_config import QuantizationConf
 from vllm.model_executor.layers.quantization.utils.layer_utils import replace_parameter
 from vllm.model_executor.utils import set_weight_attrs
 
+from . import allreduce as _allreduce  # noqa: F401  (registers torch.ops.grinqh.row_parallel_linear)
 from .kernel import grinqh_gemm_or_gemv  # noqa: F401  (registers torch.ops.grinqh)
 from .utils import pack_codes, unpack_checkpoint
 
@@ -231,8 +232,28 @@ class GRINQHLinearMethod(LinearMethodBase):
         packed = pack_codes(codes, max_bits=self.quant_config.num_bits)
         replace_parameter(layer, layer.grinqh_weight_param_name, packed)
         layer.grinqh_use_marlin = False
+        # GRINQH_FUSED_ALLREDUCE=1: a row-parallel layer whose output vLLM would
+        # all-reduce does the reduction itself (grinqh.allreduce.row_parallel_linear:
+        # single rows in one GEMV + NVLink-sum kernel). Layers built with
+        # reduce_results=False (the model reduces elsewhere) are left alone.
+        layer.grinqh_fused_allreduce = False
+        if (os.environ.get("GRINQH_FUSED_ALLREDUCE") == "1" and hasattr(layer, "input_is_parallel")
+                and getattr(layer, "reduce_results", False) and int(getattr(layer, "tp_size", 1) or 1) > 1):
+            layer.reduce_results = False
+            layer.grinqh_fused_allreduce = True
+            # the peer buffers are set up here, at load time (collective over the TP
+            # group, same layer order on every rank), never inside graph capture
+            from .allreduce import tp_peers
+            tp_peers(packed.device, 4 * layer.original_n)
 
     def apply(self, layer: torch.nn.Module, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if getattr(layer, "grinqh_fused_allreduce", False):
+            # vLLM passes the bias on rank 0 only; the fused op adds the full bias once
+            full_bias = None if getattr(layer, "skip_bias_add", False) else getattr(layer, "bias", None)
+            return torch.ops.grinqh.row_parallel_linear(
+                x, getattr(layer, layer.grinqh_weight_param_name), layer.weight_scale, full_bias,
+                self.quant_config.num_bits, self.quant_config.group_size, layer.original_n,
+                list(self.layer_thresholds))
         return torch.ops.grinqh.gemm_or_gemv(
             x,
             getattr(layer, layer.grinqh_weight_param_name),
