@@ -156,9 +156,40 @@ def _worker(rank, world, port, q):
             e1.record()
             torch.cuda.synchronize(dev)
             times[name] = e0.elapsed_time(e1) * 1e3 / 200
-        t = torch.tensor([times["fused"], times["gemv+nccl"]], device=dev)
+        # the same calls replayed from CUDA graphs (no host launch cost): the fused
+        # kernel against the GEMV of the same slice alone, i.e. what the in-kernel sum adds
+        def gemv_only():
+            return torch.ops.grinqh.gemm_or_gemv(xd, wr, sr, None, b, 128, N // 4, th, False)
+
+        st = torch.cuda.Stream(dev)
+        for name, fn in (("fused graph", fused), ("gemv graph", gemv_only)):
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                fn()
+            torch.cuda.current_stream(dev).wait_stream(st)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                for _ in range(50):
+                    fn()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            gr.replay()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(4):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            times[name] = e0.elapsed_time(e1) * 1e3 / 200
+            del gr
+        t = torch.tensor([times["fused"], times["gemv+nccl"], times["fused graph"], times["gemv graph"]], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        lines.append(f"K={K} N={N} TP={world}: fused {t[0].item():.1f} us, gemv + NCCL all-reduce {t[1].item():.1f} us")
+        lines.append(f"K={K} N={N} TP={world}: eager fused {t[0].item():.1f} us, eager gemv + NCCL all-reduce "
+                     f"{t[1].item():.1f} us; graph fused {t[2].item():.1f} us, graph gemv alone {t[3].item():.1f} us")
         from grinqh._ext import cabi
         import ctypes
         n_to = ctypes.c_uint(0)
