@@ -403,13 +403,16 @@ def test_dense_skinny_gemm(M, K, N, dtype, b):
     assert torch.equal(y, y2), "skinny GEMM is not deterministic"
 
 
-@pytest.mark.parametrize("M,K,N", [(512, 256, 4128), (600, 384, 320), (1024, 1024, 1024), (520, 256, 4112)])
+@pytest.mark.parametrize("M,K,N", [(512, 256, 4128), (600, 384, 320), (1024, 1024, 1024), (520, 256, 4112),
+                                   (128, 14336, 1024), (200, 4096, 2048), (65, 2048, 1056)])
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("b", [8, 4, 2, 6])
 def test_dense_two_pass_gemm(M, K, N, dtype, b):
-    """Rows >= 512 dequantize once to dtype(w*s) and run the TMA-fed tcgen05 GEMM: a
-    partial last column tile (N = 4128), a row tail (600) and several tiles each way;
-    N/16 odd (4112) takes the fused GEMM instead."""
+    """Rows >= 512 (or few output tiles) dequantize once to dtype(w*s) and run the
+    TMA-fed tcgen05 GEMM: a partial last column tile (N = 4128), a row tail (600) and
+    several tiles each way; N/16 odd (4112) takes the fused GEMM instead. Few output
+    tiles split K over the SMs (1024^3, 128 x 14336 x 1024, 200 rows, 65 rows with a
+    partial column tile), the splits added in order by the last one."""
     from grinqh.kernel import grinqh_gemm_or_gemv
     from grinqh.utils import pack_codes
     rng = np.random.default_rng(M + 3 * K + N + b)
@@ -426,3 +429,6 @@ def test_dense_two_pass_gemm(M, K, N, dtype, b):
     ref = O.gemm_or_gemv(O.to_f32(xs, dtype), codes, O.to_f32(s_store, dtype), O.to_f32(bias, dtype), b, 128,
                          [0.0] * 4, dtype)
     assert_parity(f32(y), O.to_f32(ref, dtype))
+    y2 = grinqh_gemm_or_gemv(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128,
+                             N // 4, [0.0] * 4)
+    assert torch.equal(y, y2), "two-pass GEMM is not deterministic"

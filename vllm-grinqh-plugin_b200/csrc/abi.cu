@@ -231,8 +231,10 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   // runs the generic kernel, and this query does not see the pointers: cover both
   const size_t generic = workspace_for(plan_decode(M, K, N, km, sms));
   if (use_bf16_gemm(km, M, K, N, sms)) {
-    // the dtype(w * s) buffer sits after the ticket region, which it never touches
-    const size_t a = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
+    // the dtype(w * s) buffer sits after the ticket region, then the split-K sums
+    const int splits = bf16_gemm_splits(M, K, N, sms);
+    const size_t a = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256) +
+                     align_up(bf16_gemm_slot_bytes(M, N, splits), 256);
     return a > generic ? a : generic;
   }
   if (use_skinny(km, M, K, N, group_size)) {
@@ -331,7 +333,9 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   }
 
   if (use_bf16_gemm(km, M, K, N, sms) && bf16_gemm_supported(M, K, N, group, x, w, s, y)) {
-    const size_t need = kTicketBytes + align_up(bf16_gemm_buffer_bytes(K, N), 256);
+    const int splits = bf16_gemm_splits(M, K, N, sms);
+    const size_t wbuf_bytes = align_up(bf16_gemm_buffer_bytes(K, N), 256);
+    const size_t need = kTicketBytes + wbuf_bytes + align_up(bf16_gemm_slot_bytes(M, N, splits), 256);
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
     GRINQH_REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
@@ -346,6 +350,16 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     g.K = (int)K;
     g.N = (int)N;
     g.group = group;
+    g.splits = splits;
+    if (splits > 1) {  // one ticket per output tile at the start of the workspace
+      g.counters = static_cast<unsigned*>(workspace);
+      g.slots = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes + wbuf_bytes);
+      const size_t tiles = (size_t)((M + 255) / 256) * (size_t)((N + 255) / 256);
+      if (!zeroed) {
+        const cudaError_t e = cudaMemsetAsync(g.counters, 0, tiles * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+      }
+    }
     return launch_bf16_gemm(g, dtype, max_bits / 2, stream);
   }
 

@@ -123,6 +123,12 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint32_t* __restrict
 }
 
 // ---------------------------------------------------------------- pass 2: x @ W
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                   const __grid_constant__ CUtensorMap tmap_w,
@@ -141,7 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BM;
   const int n0 = blockIdx.y * BN;
-  const int nk = a.K / BK;
+  // K steps of this split (blockIdx.z of a.splits; the planner leaves none empty)
+  const int nk_all = a.K / BK;
+  const int per = (nk_all + a.splits - 1) / a.splits;
+  const int q_begin = blockIdx.z * per;
+  const int nk = max(0, min(nk_all, q_begin + per) - q_begin);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -166,9 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
         const int s = q % STAGES;
         if (q >= STAGES) mbar_wait(&empty[s], ((q / STAGES) - 1) & 1);
         mbar_arrive_expect_tx(&full[s], kStageA + kStageB);
-        tma_load_2d(sA + s * kStageA, &tmap_x, q * BK, m0, &full[s]);
+        tma_load_2d(sA + s * kStageA, &tmap_x, (q_begin + q) * BK, m0, &full[s]);
 #pragma unroll
-        for (int b = 0; b < BN / 64; ++b) tma_load_2d(sB + s * kStageB + b * kBoxB, &tmap_w, n0 + 64 * b, q * BK, &full[s]);
+        for (int b = 0; b < BN / 64; ++b)
+          tma_load_2d(sB + s * kStageB + b * kBoxB, &tmap_w, n0 + 64 * b, (q_begin + q) * BK, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -205,30 +216,100 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     const int m = m0 + half * 128 + quarter * 32 + lane;
     T* y = static_cast<T*>(a.y);
     const T* bias = static_cast<const T*>(a.bias);
+    // 8 columns (16 bytes of y) of row mm at a time: cast, bias, one 16-byte store
+    auto store8 = [&](int mm, int n, const float* v) {
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        T lo = Act<T>::from_f(v[2 * t]);
+        T hi = Act<T>::from_f(v[2 * t + 1]);
+        if (bias) {
+          lo = Act<T>::from_f(Act<T>::to_f(lo) + Act<T>::to_f(bias[n + 2 * t]));
+          hi = Act<T>::from_f(Act<T>::to_f(hi) + Act<T>::to_f(bias[n + 2 * t + 1]));
+        }
+        o[t] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+      }
+      *reinterpret_cast<uint4*>(y + (size_t)mm * a.N + n) = make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    const bool split = a.splits > 1;
 #pragma unroll 1
     for (int cc = 0; cc < BN / 32; ++cc) {
       uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + half * BN + cc * 32, r);
-      tmem_ld_wait();
+      if (nk > 0) {
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + half * BN + cc * 32, r);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) r[t] = 0u;
+      }
       if (m >= a.M) continue;
       const int nb = n0 + 32 * cc;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {  // 8 columns (16 bytes) at a time
+      for (int e = 0; e < 4; ++e) {  // N is a multiple of 16, so runs of 8 are whole
         const int n = nb + 8 * e;
-        if (n >= a.N) break;  // N is a multiple of 16, so runs of 8 are whole
-        uint32_t o[4];
+        if (n >= a.N) break;
+        if (split) {  // this split's fp32 sums: slots[split][m][n]
+          float4* dst = reinterpret_cast<float4*>(a.slots + ((size_t)blockIdx.z * a.M + m) * a.N + n);
+          __stcg(dst, make_float4(__uint_as_float(r[8 * e]), __uint_as_float(r[8 * e + 1]), __uint_as_float(r[8 * e + 2]),
+                                  __uint_as_float(r[8 * e + 3])));
+          __stcg(dst + 1, make_float4(__uint_as_float(r[8 * e + 4]), __uint_as_float(r[8 * e + 5]),
+                                      __uint_as_float(r[8 * e + 6]), __uint_as_float(r[8 * e + 7])));
+        } else {
+          float v[8];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          T lo = Act<T>::from_f(__uint_as_float(r[8 * e + 2 * t]));
-          T hi = Act<T>::from_f(__uint_as_float(r[8 * e + 2 * t + 1]));
-          if (bias) {
-            lo = Act<T>::from_f(Act<T>::to_f(lo) + Act<T>::to_f(bias[n + 2 * t]));
-            hi = Act<T>::from_f(Act<T>::to_f(hi) + Act<T>::to_f(bias[n + 2 * t + 1]));
-          }
-          o[t] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+          for (int t = 0; t < 8; ++t) v[t] = __uint_as_float(r[8 * e + t]);
+          store8(m, n, v);
         }
-        *reinterpret_cast<uint4*>(y + (size_t)m * a.N + n) = make_uint4(o[0], o[1], o[2], o[3]);
       }
+    }
+    if (split) {
+      // Split-K fix-up, shared by the tile's splits: each one arrives on the tile's
+      // ticket, waits until every split has written its sums (the planner keeps the
+      // grid within one wave, so they are all resident; the wait is bounded), then adds
+      // its share of the tile's rows over the splits in split order and stores them.
+      // A second count on the same ticket lets the last one reset it.
+      constexpr int kEpiThreads = 32 * kEpiWarps;
+      const int et = threadIdx.x - 64;  // 0 .. kEpiThreads - 1
+      unsigned* ticket = a.counters + blockIdx.x * gridDim.y + blockIdx.y;
+      __threadfence();
+      named_barrier(1, kEpiThreads);
+      if (et == 0) {
+        atomicAdd(ticket, 1u);
+        if (ld_acquire_gpu(ticket) < (unsigned)a.splits) {
+          const uint64_t t0 = globaltimer_ns();
+          for (uint32_t it = 1;; ++it) {
+            __nanosleep(128);
+            if (ld_acquire_gpu(ticket) >= (unsigned)a.splits) break;
+            if ((it & 255u) == 0) {
+              if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u) break;
+              if (globaltimer_ns() - t0 > kWaitNs) {
+                atomicAdd(&g_wait_timeouts, 1u);
+                break;
+              }
+            }
+          }
+        }
+      }
+      named_barrier(1, kEpiThreads);
+      __threadfence();
+      const int rows = min(BM, a.M - m0);
+      const int r0 = (int)((int64_t)rows * blockIdx.z / a.splits);
+      const int r1 = (int)((int64_t)rows * (blockIdx.z + 1) / a.splits);
+      const int chunks = min(BN, a.N - n0) / 8;  // 8-column runs of this tile
+      for (int i = et; i < (r1 - r0) * chunks; i += kEpiThreads) {
+        const int mm = m0 + r0 + i / chunks;
+        const int n = n0 + 8 * (i % chunks);
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int z = 0; z < a.splits; ++z) {
+          const float4* src = reinterpret_cast<const float4*>(a.slots + ((size_t)z * a.M + mm) * a.N + n);
+          const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+          v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+          v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
+        }
+        store8(mm, n, v);
+      }
+      named_barrier(1, kEpiThreads);
+      if (et == 0 && atomicAdd(ticket, 1u) == 2u * a.splits - 1u) *ticket = 0u;  // ready for the next launch
     }
   }
   tc_fence_before();
@@ -290,7 +371,7 @@ int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
   auto kern = gemm_bf16_kernel<T>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN));
+  const dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN), (unsigned)a.splits);
   kern<<<grid, kThreads, kSmemBytes, st>>>(tmap_x, tmap_w, a);
   return check_launch("gemm_bf16");
 }
@@ -317,6 +398,29 @@ bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void*
 }
 
 size_t bf16_gemm_buffer_bytes(int64_t K, int64_t N) { return (size_t)K * (size_t)N * 2; }
+
+int bf16_gemm_splits(int64_t M, int64_t K, int64_t N, int sm_count) {
+  // one CTA per SM (about 197 KB of shared memory): split K when the output tiles
+  // leave most SMs idle, keeping at least 4 K steps per split, no split empty and the
+  // whole grid within one wave (the splits of a tile wait for each other)
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int64_t nk = K / BK;
+  const int64_t sms = sm_count > 0 ? sm_count : 148;
+  // the fix-up writes and re-reads splits x M x N fp32 sums: with a quarter of the SMs
+  // busy already and short K (under 128 steps) that costs more than it saves (B200:
+  // 4096 x 6144 at M = 512, 4096 x 4096 at M = 1024)
+  if (tiles > sms / 4 && nk < 128) return 1;
+  int64_t splits = sms / (tiles > 0 ? tiles : 1);
+  if (splits > nk / 4) splits = nk / 4;
+  if (splits < 1) splits = 1;
+  const int64_t per = (nk + splits - 1) / splits;
+  splits = (nk + per - 1) / per;
+  return (int)splits;
+}
+
+size_t bf16_gemm_slot_bytes(int64_t M, int64_t N, int splits) {
+  return splits > 1 ? (size_t)splits * (size_t)M * (size_t)N * sizeof(float) : 0;
+}
 
 int launch_bf16_gemm(const Bf16GemmArgs& a, int dtype, int nz, cudaStream_t st) {
   if (dtype == GRINQH_BF16) {
