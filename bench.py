@@ -22,6 +22,7 @@ time is the max over ranks and the value sums all ranks' bytes.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -276,20 +277,42 @@ def run_ours(args, rank, world, dev):
     hbm_peak, tc_peak, peak_src = _peaks()
     achieved = per[name] / (kern_ms / 1e3) / 1e9
 
-    # ---- end to end through the public op with host buffers: pinned H2D of each
-    # step's activations, the four linears, D2H of the outputs, per step
-    host_x = {n: xs[n].cpu().pin_memory() for n in SHAPES}
-    host_y = {n: torch.empty((M, SHAPES[n][1]), dtype=torch.bfloat16).pin_memory() for n in SHAPES}
-    dev_x = {n: torch.empty_like(xs[n]) for n in SHAPES}
-    h2d = sum(t.numel() * t.element_size() for t in host_x.values())
-    d2h = sum(t.numel() * t.element_size() for t in host_y.values())
+    # ---- end to end through the C ABI (include/grinqh_b200.h) with host buffers: per
+    # step, one pinned H2D of the step's activations (the four linears' x, packed back
+    # to back), the four grinqh_gemm_or_gemv calls writing into one output buffer, and
+    # one D2H of that buffer
+    from grinqh._ext import cabi, check, thresholds_arg, GRINQH_BF16, MODE_AUTO
+    lib = cabi()
+    names = list(SHAPES)
+    x_off, y_off, nx, ny = {}, {}, 0, 0
+    for n in names:
+        K, N = SHAPES[n]
+        x_off[n], y_off[n] = nx, ny
+        nx, ny = nx + M * K, ny + M * N
+    host_x = torch.empty(nx, dtype=torch.bfloat16).pin_memory()
+    for n in names:
+        host_x[x_off[n]:x_off[n] + M * SHAPES[n][0]].copy_(xs[n].reshape(-1).cpu())
+    host_y = torch.empty(ny, dtype=torch.bfloat16).pin_memory()
+    dev_x = torch.empty(nx, dtype=torch.bfloat16, device=dev)
+    dev_y = torch.empty(ny, dtype=torch.bfloat16, device=dev)
+    ws_bytes = max(lib.grinqh_workspace_size(M, K, N, bits, GROUP, MODE_AUTO) for K, N in SHAPES.values())
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)  # tickets stay zero between calls
+    th_args = {n: thresholds_arg(ths[n]) for n in names}
+    workspace_zeroed = 0x100  # GRINQH_WORKSPACE_ZEROED
+    h2d = host_x.numel() * host_x.element_size()
+    d2h = host_y.numel() * host_y.element_size()
 
     def e2e_step(li):
-        for n in SHAPES:
-            dev_x[n].copy_(host_x[n], non_blocking=True)
-        outs = step(layers[li], dev_x)
-        for n, o in zip(SHAPES, outs):
-            host_y[n].copy_(o, non_blocking=True)
+        dev_x.copy_(host_x, non_blocking=True)
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        for n in names:
+            K, N = SHAPES[n]
+            w, s = layers[li][n]
+            check(lib.grinqh_gemm_or_gemv(dev_x.data_ptr() + 2 * x_off[n], GRINQH_BF16, M, K, w.data_ptr(),
+                                          s.data_ptr(), None, bits, GROUP, N, th_args[n],
+                                          MODE_AUTO | workspace_zeroed, dev_y.data_ptr() + 2 * y_off[n],
+                                          ws.data_ptr(), ws.numel(), st), f"e2e {n}")
+        host_y.copy_(dev_y, non_blocking=True)
 
     with torch.cuda.stream(stream):
         ge = []
