@@ -282,7 +282,7 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
     return launch_m1tc(g, plan, dtype, max_bits / 2, stream);
   }
 
-  if (use_m1(km, M, K, N, group) && m1_pointers_ok(w, s)) {
+  if (use_m1(km, M, K, N, group) && m1_pointers_ok(w, s) && m1_plan_fits(plan_m1(K, N, group, sms))) {
     const M1Plan plan = plan_m1(K, N, group, sms);
     const size_t need = workspace_for(plan);
     if (need > 0 && (workspace == nullptr || workspace_bytes < need))
@@ -467,7 +467,7 @@ extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const 
                  rank, world, kArMaxRanks);
   GRINQH_REQUIRE(buffers && N <= n_cap, "peer buffers hold %lld columns, N is %lld", (long long)n_cap, (long long)N);
   for (int r = 0; r < world; ++r) GRINQH_REQUIRE(buffers[r] && aligned(buffers[r], 256), "peer buffer %d", r);
-  if (!m1_supported(1, K, N, group) || !m1_pointers_ok(w, s))
+  if (!m1_supported(1, K, N, group) || !m1_pointers_ok(w, s) || !m1_plan_fits(plan_m1(K, N, group, sms)))
     return set_error(GRINQH_ERR_UNSUPPORTED, "fused all-reduce: shape or alignment not supported by the GEMV");
   const bool zeroed = (mode & GRINQH_WORKSPACE_ZEROED) != 0;
   const M1Plan plan = plan_m1(K, N, group, sms);

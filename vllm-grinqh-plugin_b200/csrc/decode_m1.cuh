@@ -47,6 +47,9 @@ inline bool m1_pointers_ok(const void* w, const void* s) {
   return (reinterpret_cast<uintptr_t>(w) % 8) == 0 && (reinterpret_cast<uintptr_t>(s) % 4) == 0;
 }
 M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
+// the plan's shared memory fits one CTA (rows_per_cta grows with K when N is so wide
+// that the column slices alone fill the GPU)
+inline bool m1_plan_fits(const M1Plan& p) { return p.smem_bytes <= 227u * 1024u; }
 int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st, bool allreduce = false);
 inline size_t m1_allreduce_buffer_bytes(int world, int64_t n_cap) {
   return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(float);

@@ -75,6 +75,9 @@ extern "C" int grinqh_gemv_noalloc(const void* x, int dtype, int64_t K, const ui
   cudaGetDevice(&dev);
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
   const M1Plan plan = plan_m1(K, N, group, sms);
+  if (!m1_plan_fits(plan))
+    return set_error(GRINQH_ERR_UNSUPPORTED, "K=%lld N=%lld: the GEMV's shared memory does not fit one CTA (use "
+                     "grinqh_gemm_or_gemv)", (long long)K, (long long)N);
   const size_t counters = round256(plan.counter_bytes);
   const size_t need = counters + round256(plan.slot_bytes);
   if (need > kNoAllocScratchBytes)
