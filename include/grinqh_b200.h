@@ -180,9 +180,10 @@ int grinqh_gemv_noalloc(const void *x_dev, int dtype, int64_t K, const uint32_t 
  * Replaces, for M = 1, the plugin's apply (grinqh/grinqh.py:236-247) followed by vLLM's
  * row-parallel all-reduce of the partial outputs (vllm/model_executor/layers/linear.py,
  * RowParallelLinear.forward): each rank computes the graded GEMV of its K slice and the
- * kernel that does so also sums the ranks' fp32 partials over NVLink (plain peer
- * stores into every rank's buffer, per-launch flags, bounded waits) and writes the
- * summed y (+ bias, applied once) on every rank, the same bits on every rank.
+ * kernel that does so also sums the ranks' fp32 partials over NVLink (plain 64-bit
+ * peer stores of {partial, launch epoch} into every rank's buffer, bounded waits on
+ * the epochs) and writes the summed y (+ bias, applied once) on every rank, the same
+ * bits on every rank.
  *   - Every rank owns one peer buffer of grinqh_allreduce_buffer_bytes(world, n_cap)
  *     bytes from grinqh_allreduce_buffer_alloc (zeroed); the ranks exchange
  *     grinqh_ipc_get_handle handles (64 bytes) and open each other's with

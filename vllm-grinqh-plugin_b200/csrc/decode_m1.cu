@@ -192,69 +192,94 @@ __device__ __forceinline__ void warp_chunk(const M1Args& a, int tile, int kb, in
 }
 
 // ---------------------------------------------------------------- fused all-reduce
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Partials travel as 64-bit words {fp32 bits, epoch}: a naturally aligned 64-bit
+// store is single-copy atomic, so a reader that sees this launch's epoch in a word
+// also sees the value stored with it, without a fence or a separate flag.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
-// Runs in every finalizing CTA (one per column slice) after it has written its
-// slice's sums into every rank's buffer. The last of them on this rank (ticket):
-// announces the epoch to every rank, waits (bounded) until every rank has announced
-// it here, then adds the ranks' partials in rank order -- the same order on every
-// rank, so all ranks get the same bits -- adds the bias and writes y.
+// Runs in the CTA that finalises column slice `tile`, after it has stored the slice's
+// sums into every rank's buffer: waits (bounded) until every rank's partial of each of
+// this thread's columns carries this launch's epoch, then adds them in rank order --
+// the same order on every rank, so all ranks get the same bits -- adds the bias and
+// writes y. The slices finalise independently; a waiting CTA waits only on the peer
+// CTAs that finalise the same slice, which wait on nothing on their own GPU.
 template <typename T>
-__device__ void allreduce_tail(const M1Args& a, unsigned epoch, int* s_flag) {
+__device__ void allreduce_tail(const M1Args& a, int tile, unsigned epoch) {
+  constexpr int kH = kSliceN / kThreads;
   const M1AllReduce& ar = a.ar;
-  unsigned* ctrl = reinterpret_cast<unsigned*>(ar.buf[ar.rank]);
-  __syncthreads();  // this CTA's partial stores are issued
-  if (threadIdx.x == 0) {
-    __threadfence_system();  // ... and visible to every rank before the ticket
-    *s_flag = atomicAdd(ctrl + 1, 1u) == gridDim.x - 1u;  // one finalizing CTA per slice
+  const int n16 = a.N >> 4;
+  const unsigned long long* parts = reinterpret_cast<const unsigned long long*>(ar.buf[ar.rank] + kArParts) +
+                                    (size_t)(epoch & 1u) * ar.world * ar.n_cap;
+  int nn[kH];
+  bool ok[kH];
+#pragma unroll
+  for (int h = 0; h < kH; ++h) {  // the columns store_y wrote for this thread
+    const int col = threadIdx.x + h * kThreads;
+    const int jx = tile * kSliceW + col % kSliceW;
+    ok[h] = jx < n16;
+    nn[h] = (col / kSliceW) * n16 + jx;
   }
-  __syncthreads();
-  if (!*s_flag) return;
-  __threadfence_system();
-  if (threadIdx.x < (unsigned)ar.world) {
-    const int r = threadIdx.x;
-    st_release_sys(reinterpret_cast<unsigned*>(ar.buf[r] + kArFlags) + ar.rank, epoch);
-    const unsigned* mine = reinterpret_cast<const unsigned*>(ar.buf[ar.rank] + kArFlags) + r;
-    if (ld_acquire_sys(mine) != epoch) {
-      const uint64_t t0 = globaltimer_ns();
-      for (uint32_t it = 1;; ++it) {
-        __nanosleep(64);
-        if (ld_acquire_sys(mine) == epoch) break;
-        if ((it & 255u) == 0) {
-          // after any wait of this library gave up, give up at once (the output is
-          // invalid anyway and the host sees the count); else after kWaitNs
-          if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u) break;
-          if (globaltimer_ns() - t0 > kWaitNs) {  // a rank never arrived
-            atomicAdd(&g_wait_timeouts, 1u);
-            break;
-          }
+  // two ranks at a time (2 * kH words in flight), each added in rank order
+  float v[kH];
+#pragma unroll
+  for (int h = 0; h < kH; ++h) v[h] = 0.f;
+  uint64_t t0 = 0;
+  bool gave_up = false;
+  for (int r0 = 0; r0 < ar.world && !gave_up; r0 += 2) {
+    const int nr = min(2, ar.world - r0);
+    unsigned long long q[2][kH];
+    for (uint32_t it = 0;; ++it) {
+      bool all = true;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int h = 0; h < kH; ++h)
+          if (j < nr && ok[h] && (it == 0 || (unsigned)(q[j][h] >> 32) != epoch))
+            q[j][h] = ld_relaxed_sys_u64(parts + (size_t)(r0 + j) * ar.n_cap + nn[h]);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int h = 0; h < kH; ++h)
+          if (j < nr && ok[h] && (unsigned)(q[j][h] >> 32) != epoch) all = false;
+      if (all) break;
+      if (t0 == 0) t0 = globaltimer_ns();
+      if ((it & 63u) == 63u) {
+        // after any wait of this library gave up, give up at once (the output is
+        // invalid anyway and the host sees the count); else after kWaitNs
+        if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u ||
+            globaltimer_ns() - t0 > kWaitNs) {  // a rank never arrived
+          if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) == 0u) atomicAdd(&g_wait_timeouts, 1u);
+          gave_up = true;
+          break;
         }
       }
+      __nanosleep(32);
     }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int h = 0; h < kH; ++h)
+        if (j < nr) v[h] += __uint_as_float((unsigned)q[j][h]);
   }
-  __syncthreads();
-  const float* parts = reinterpret_cast<const float*>(ar.buf[ar.rank] + kArParts) +
-                       (size_t)(epoch & 1u) * ar.world * ar.n_cap;
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
-  for (int n = threadIdx.x; n < a.N; n += blockDim.x) {
-    float v = 0.f;
-    for (int r = 0; r < ar.world; ++r) v += __ldcv(parts + (size_t)r * ar.n_cap + n);
-    T out = Act<T>::from_f(v);
-    if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[n]));
-    y[n] = out;
+#pragma unroll
+  for (int h = 0; h < kH; ++h) {
+    if (!ok[h]) continue;
+    T out = Act<T>::from_f(v[h]);
+    if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[nn[h]]));
+    y[nn[h]] = out;
   }
-  if (threadIdx.x == 0) {
-    ctrl[1] = 0u;      // ticket ready for the next launch
-    ctrl[0] = epoch;   // read by the next launch after griddepcontrol.wait
-  }
+  // read by the next launch after griddepcontrol.wait (every finalising CTA writes the
+  // same value)
+  if (threadIdx.x == 0) *reinterpret_cast<unsigned*>(ar.buf[ar.rank]) = epoch;
 }
 
 template <int NZ, typename T, bool kAR>
@@ -331,7 +356,9 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     const int nn = c * n16 + jx;
     if constexpr (kAR) {  // this rank's partial, into every rank's buffer (NVLink stores)
       const size_t off = ((size_t)(ar_epoch & 1u) * a.ar.world + a.ar.rank) * a.ar.n_cap + nn;
-      for (int r = 0; r < a.ar.world; ++r) __stcg(reinterpret_cast<float*>(a.ar.buf[r] + kArParts) + off, v);
+      const unsigned long long word = ((unsigned long long)ar_epoch << 32) | __float_as_uint(v);
+      for (int r = 0; r < a.ar.world; ++r)
+        st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.ar.buf[r] + kArParts) + off, word);
       return;
     }
     T out = Act<T>::from_f(v);
@@ -342,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   if (nclu == 1) {
 #pragma unroll
     for (int h = 0; h < kSliceN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
-    if constexpr (kAR) allreduce_tail<T>(a, ar_epoch, &s_last);
+    if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
     return;
   }
   const int clu = split / csize;
@@ -370,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     store_y(col, v);
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
-  if constexpr (kAR) allreduce_tail<T>(a, ar_epoch, &s_last);
+  if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
 }
 
 template <int NZ, typename T, bool kAR>

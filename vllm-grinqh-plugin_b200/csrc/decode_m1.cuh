@@ -8,11 +8,11 @@
 namespace grinqh {
 
 // Fused all-reduce over the tensor-parallel ranks' peer buffers (grinqh_gemv_allreduce).
-// Buffer of a rank: [0] epoch of its last completed launch, [1] launch ticket; at
-// kArFlags the epoch each rank last published into it; at kArParts the partial sums
-// [2 (epoch parity)][world][n_cap] fp32 written by every rank.
+// Buffer of a rank: [0] epoch of its last completed launch; at kArParts the partial
+// sums [2 (epoch parity)][world][n_cap], each a 64-bit word {fp32 bits, epoch} written
+// by the rank that computed it (the epoch in the word tells the reader it is current).
 constexpr int kArMaxRanks = 8;
-constexpr size_t kArFlags = 256, kArParts = 1024;
+constexpr size_t kArParts = 256;
 struct M1AllReduce {
   unsigned char* buf[kArMaxRanks];  // every rank's buffer as mapped in this process
   int rank, world, n_cap;
@@ -52,7 +52,7 @@ M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
 inline bool m1_plan_fits(const M1Plan& p) { return p.smem_bytes <= 227u * 1024u; }
 int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st, bool allreduce = false);
 inline size_t m1_allreduce_buffer_bytes(int world, int64_t n_cap) {
-  return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(float);
+  return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(uint64_t);
 }
 
 }  // namespace grinqh
