@@ -1,5 +1,5 @@
 """The fused row-parallel kernel (torch.ops.grinqh.gemv_allreduce) with a single
-rank: its peer-buffer path (publish, epoch flag, ordered sum) must give exactly the
+rank: its peer-buffer path (epoch-tagged partials, bounded wait, ordered sum) must give exactly the
 plain single-row GEMV's bits, over many consecutive launches (both buffer parities)
 and under CUDA-graph replay. Runs on one GPU; the two-GPU test is
 test_tp_fused_allreduce.py."""
