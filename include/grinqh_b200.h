@@ -80,9 +80,11 @@ int grinqh_abi_version(void);
 const char *grinqh_status_string(int status);
 const char *grinqh_last_error(void);
 
-/* Number of pipeline waits (mbarrier) in this library's kernels on the current
- * device that hit their iteration limit since the last call, then reset to 0.
- * Non-zero means a kernel gave up waiting and its output is not valid. Synchronous.
+/* Number of bounded waits in this library's kernels on the current device (pipeline
+ * mbarriers, split-K fix-ups, the fused all-reduce's wait for the other ranks) that
+ * gave up since the last call, then reset to 0. Non-zero means a kernel gave up
+ * waiting and its output is not valid; once one wait has given up, later waits give
+ * up at once until this call clears the count. Synchronous.
  * (No reference counterpart: the reference's Triton kernels have no device waits.) */
 int grinqh_take_error_flags(unsigned *timeouts);
 
@@ -165,7 +167,9 @@ int grinqh_prefill_gemm(const void *x_dev, int dtype, int64_t M, int64_t K,
  * loads the library holds that array until the process exits.
  *   - The first call on a device looks up the array's device address (once per
  *     device, with that device current); make that first call before any stream
- *     capture.
+ *     capture. The address is kept for the life of the process and belongs to the
+ *     device's primary context: after cudaDeviceReset on a device, do not call this
+ *     entry point on that device again.
  *   - A launch plan whose scratch would exceed 256 KiB returns
  *     GRINQH_ERR_WORKSPACE (the kernel's K split keeps every shape below it on a
  *     148-SM B200, so this is a guard).
@@ -191,8 +195,10 @@ int grinqh_gemv_noalloc(const void *x_dev, int dtype, int64_t K, const uint32_t 
  *     process (buffers_dev[rank] the own one). At most 8 ranks.
  *   - Every rank must make the same sequence of calls on its buffer (launch epochs are
  *     counted on the device, so calls can be recorded in CUDA graphs). A rank that
- *     never arrives makes the others give up after about 2 s: grinqh_take_error_flags
- *     then reports a non-zero count and y is not valid.
+ *     never arrives makes the others give up after GRINQH_ALLREDUCE_WAIT_MS
+ *     milliseconds (environment, read on every call; default 2000):
+ *     grinqh_take_error_flags then reports a non-zero count, y is not valid, and
+ *     every rank should call grinqh_take_error_flags before its next launch.
  *   - workspace / mode as for grinqh_gemm_or_gemv with M = 1 (GRINQH_WORKSPACE_ZEROED
  *     honoured); thresholds: 4 host floats. */
 size_t grinqh_allreduce_buffer_bytes(int world, int64_t n_cap);

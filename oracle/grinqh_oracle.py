@@ -17,7 +17,7 @@ __all__ = [
     "bf16_bits_to_f32", "f32_to_bf16_bits", "to_f32", "round_to_dtype",
     "preshuffle", "postshuffle", "shifted_words", "pack_words", "pack_codes",
     "unpack", "unpack_codes", "grade", "zone_bias", "bias_table",
-    "masked_codes", "graded_gemv", "union_gemv", "looped_gemv", "dense",
+    "masked_codes", "graded_gemv", "union_gemv", "looped_gemv", "graded_rows", "dense_weight", "dense",
     "gemm_or_gemv", "ct_pack_to_int32", "ct_unpack_from_int32",
     "rtn_quantize", "make_activations", "quantile_thresholds",
 ]
@@ -220,14 +220,47 @@ def looped_gemv(x_f32: np.ndarray, codes, scales_f32, thresholds, max_bits, grou
                      for m in range(x.shape[0])])
 
 
+def graded_rows(x_f32: np.ndarray, codes: np.ndarray, scales_f32: np.ndarray,
+                thresholds, max_bits: int, group_size: int, k_chunk: int = 512) -> np.ndarray:
+    """Same result as :func:`looped_gemv` (every row of x graded by itself,
+    grinqh/kernel.py:100-158 per token), evaluated for many rows at once: the masked
+    weight of row k depends only on that row's zone mask, so for each mask value that
+    occurs the rows' activations with that mask multiply one masked weight matrix.
+    Processed in K chunks of ``k_chunk`` rows (a multiple of ``group_size``) so the
+    float64 matrices stay small. Float64 accumulation."""
+    x = np.asarray(x_f32, dtype=np.float32).reshape(-1, np.asarray(x_f32).shape[-1])
+    m_all = grade(x, thresholds, max_bits)
+    k_total, n = codes.shape
+    assert k_chunk % group_size == 0
+    y = np.zeros((x.shape[0], n), dtype=np.float64)
+    bias = bias_table(max_bits)
+    for k0 in range(0, k_total, k_chunk):
+        k1 = min(k_total, k0 + k_chunk)
+        s = _scales_rows(scales_f32[k0 // group_size:(k1 + group_size - 1) // group_size], k1 - k0, group_size)
+        mk = m_all[:, k0:k1]
+        for mv in np.unique(mk):
+            if mv == 0:
+                continue
+            sel = np.where(mk == mv, x[:, k0:k1], 0.0).astype(np.float64)
+            w = masked_codes(codes[k0:k1], np.full(k1 - k0, mv, dtype=np.uint8), max_bits).astype(np.float64)
+            y += sel @ ((w + bias[mv]) * s)
+    return y
+
+
+def dense_weight(codes: np.ndarray, scales_f32: np.ndarray, group_size: int, dtype: str) -> np.ndarray:
+    """``dtype(w * s)`` of the dense path (grinqh/kernel.py:586: ``w.to(dtype) * s``,
+    rounded to the activation dtype), returned exactly as float32."""
+    w = np.asarray(codes, dtype=np.float32)
+    s = np.repeat(np.asarray(scales_f32, dtype=np.float32), group_size, axis=0)[: w.shape[0]]
+    return to_f32(round_to_dtype(w * s, dtype), dtype)
+
+
 def dense(x_f32: np.ndarray, codes: np.ndarray, scales_f32: np.ndarray,
           group_size: int, dtype: str) -> np.ndarray:
     """M > 1 dense path ``grinqh_prefill_gemm_compiled`` (grinqh/kernel.py:561-587):
     ``x @ dtype(w * s)`` -- the product is rounded to the activation dtype before
     the matmul (kernel.py:586); accumulation here is float64."""
-    w = np.asarray(codes, dtype=np.float32)
-    s = np.repeat(np.asarray(scales_f32, dtype=np.float32), group_size, axis=0)[: w.shape[0]]
-    ws = to_f32(round_to_dtype(w * s, dtype), dtype).astype(np.float64)
+    ws = dense_weight(codes, scales_f32, group_size, dtype).astype(np.float64)
     return np.asarray(x_f32, dtype=np.float64) @ ws
 
 

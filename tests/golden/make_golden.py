@@ -194,7 +194,7 @@ def main():
     g["cfg_packed"], g["cfg_th"], g["cfg_y"] = _store(packed), np.array(th), _store(y)
 
     # ---- compressed-tensors checkpoint codec (loader input, grinqh.py:154-158) --------------
-    for b in (4, 8):
+    for b in (2, 4, 6, 8):
         torch.manual_seed(600 + b)
         lim = (1 << (b - 1)) - 1
         w = torch.randint(-lim - 1, lim + 1, (64, 256), dtype=torch.int8)  # (N, K) checkpoint orientation

@@ -29,8 +29,10 @@ def checkpoint_tensor(codes_nk, b):
     return torch.from_numpy(O.ct_pack_to_int32(codes_nk, b))
 
 
-@pytest.mark.parametrize("b", (4, 8))
+@pytest.mark.parametrize("b", (2, 4, 8))
 def test_golden_checkpoint_vectors(golden, b):
+    """compressed-tensors' own pack_to_int32 output -> staging codes, bit-exact (b = 6
+    checkpoints hold int8 codes, not packed words, so they have no packed vector)."""
     from grinqh.utils import unpack_checkpoint
     codes = golden[f"ct_codes_b{b}"]  # (N, K) as compressed-tensors' pack_to_int32 saw them
     src = torch.from_numpy(golden[f"ct_packed_b{b}"]).cuda()

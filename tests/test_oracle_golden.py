@@ -120,7 +120,28 @@ def test_config_like_case(golden):
     assert mx <= 4e-3 and fro <= 1e-3
 
 
-@pytest.mark.parametrize("b", [4, 8])
+@pytest.mark.parametrize("b", BITS)
+@pytest.mark.parametrize("case", ["spread", "lowest", "highest", "70_20_10", "non_monotone"])
+def test_graded_rows_equals_looped_gemv(b, case):
+    """The many-row evaluation of per-token grading (used at configs[2] sizes) equals
+    the reference-pinned one-row GEMV looped over the rows."""
+    rng = np.random.default_rng(b * 13 + len(case))
+    K, N, M = 384, 96, 7
+    codes = rng.integers(-(1 << (b - 1)), 1 << (b - 1), size=(K, N)).astype(np.int8)
+    s = O.to_f32(O.round_to_dtype(rng.random((K // 128, N)) * 0.02 + 1e-3, "bf16"), "bf16")
+    x, _ = O.make_activations(rng, M, K, dist="t3")
+    x = O.to_f32(O.round_to_dtype(x, "bf16"), "bf16")
+    ax = np.abs(x)
+    th = {"spread": O.quantile_thresholds(ax, [0.2, 0.4, 0.6, 0.8]),
+          "lowest": [-1.0, float("inf"), float("inf"), float("inf")],
+          "highest": [-1.0] * 4,
+          "70_20_10": [-1.0] + O.quantile_thresholds(ax, [0.7, 0.9, 0.9]),
+          "non_monotone": O.quantile_thresholds(ax, [0.5, 0.1, 0.9, 0.3])}[case]
+    np.testing.assert_allclose(O.graded_rows(x, codes, s, th, b, 128, k_chunk=128),
+                               O.looped_gemv(x, codes, s, th, b, 128), rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("b", BITS)
 def test_checkpoint_codec(golden, b):
     codes = golden[f"ct_codes_b{b}"]
     np.testing.assert_array_equal(O.ct_pack_to_int32(codes, b), golden[f"ct_packed_b{b}"])

@@ -403,6 +403,16 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
 }
 
 // ---------------------------------------------------------------- fused all-reduce
+// How long a fused launch waits for the other ranks' partials before it gives up and
+// counts a timeout: GRINQH_ALLREDUCE_WAIT_MS milliseconds (read on every call, default
+// 2000, at least 1).
+static unsigned long long allreduce_wait_ns() {
+  const char* e = getenv("GRINQH_ALLREDUCE_WAIT_MS");
+  long ms = e ? atol(e) : 2000;
+  if (ms < 1) ms = 1;
+  return (unsigned long long)ms * 1000000ull;
+}
+
 extern "C" size_t grinqh_allreduce_buffer_bytes(int world, int64_t max_n) {
   if (world < 1 || world > kArMaxRanks || max_n <= 0) return 0;
   return m1_allreduce_buffer_bytes(world, max_n);
@@ -489,6 +499,7 @@ extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const 
   for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
   g.ar.rank = rank;
   g.ar.world = world;
+  g.ar.wait_ns = allreduce_wait_ns();
   g.ar.n_cap = (int)n_cap;
   for (int r = 0; r < world; ++r) g.ar.buf[r] = static_cast<unsigned char*>(buffers[r]);
   if (need > 0)
@@ -499,7 +510,8 @@ extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const 
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {
   GRINQH_RETURN_IF(check_device());
-  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts() + take_skinny_timeouts() + take_bf16_gemm_timeouts();
+  const unsigned v = take_gemm_timeouts() + take_m1tc_timeouts() + take_skinny_timeouts() + take_bf16_gemm_timeouts() +
+                     take_m1_timeouts();
   if (timeouts) *timeouts = v;
   return GRINQH_OK;
 }

@@ -254,7 +254,7 @@ __device__ void allreduce_tail(const M1Args& a, int tile, unsigned epoch) {
         // after any wait of this library gave up, give up at once (the output is
         // invalid anyway and the host sees the count); else after kWaitNs
         if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u ||
-            globaltimer_ns() - t0 > kWaitNs) {  // a rank never arrived
+            globaltimer_ns() - t0 > ar.wait_ns) {  // a rank never arrived
           if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) == 0u) atomicAdd(&g_wait_timeouts, 1u);
           gave_up = true;
           break;
@@ -277,9 +277,25 @@ __device__ void allreduce_tail(const M1Args& a, int tile, unsigned epoch) {
     if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[nn[h]]));
     y[nn[h]] = out;
   }
-  // read by the next launch after griddepcontrol.wait (every finalising CTA writes the
-  // same value)
-  if (threadIdx.x == 0) *reinterpret_cast<unsigned*>(ar.buf[ar.rank]) = epoch;
+}
+
+// Every CTA of a fused launch calls this as it exits. The epoch of a launch is read by
+// each CTA when it starts, so the next epoch may only be published once every CTA of
+// the grid has started: the last CTA to finish (a grid-wide count in the buffer's
+// word 1) publishes it and clears the count. The next launch reads it after
+// griddepcontrol.wait, i.e. after this grid has completed.
+template <bool kAR>
+__device__ __forceinline__ void ar_cta_done(const M1Args& a, unsigned epoch) {
+  if constexpr (kAR) {
+    if (threadIdx.x == 0) {
+      unsigned* words = reinterpret_cast<unsigned*>(a.ar.buf[a.ar.rank]);
+      __threadfence();  // this CTA's read of the epoch is ordered before its count
+      if (atomicAdd(words + 1, 1u) == gridDim.x * gridDim.y - 1u) {
+        words[1] = 0u;
+        *reinterpret_cast<volatile unsigned*>(words) = epoch;
+      }
+    }
+  }
 }
 
 template <int NZ, typename T, bool kAR>
@@ -345,7 +361,10 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     }
   }
   cluster.sync();  // other ranks keep their shared memory alive until rank 0 has read it
-  if (crank != 0) return;
+  if (crank != 0) {
+    ar_cta_done<kAR>(a, ar_epoch);
+    return;
+  }
 
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
@@ -370,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
 #pragma unroll
     for (int h = 0; h < kSliceN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
     if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
+    ar_cta_done<kAR>(a, ar_epoch);
     return;
   }
   const int clu = split / csize;
@@ -380,7 +400,10 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(a.counters + tile, 1u) == (unsigned)(nclu - 1);
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    ar_cta_done<kAR>(a, ar_epoch);
+    return;
+  }
   __threadfence();
 #pragma unroll
   for (int h = 0; h < kSliceN / kThreads; ++h) {
@@ -398,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
   if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
+  ar_cta_done<kAR>(a, ar_epoch);
 }
 
 template <int NZ, typename T, bool kAR>
@@ -430,6 +454,13 @@ int launch_t(const M1Args& a, const M1Plan& p, cudaStream_t st) {
 }
 
 }  // namespace
+
+unsigned take_m1_timeouts() {
+  unsigned v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v)) != cudaSuccess) return 0;
+  cudaMemcpyToSymbol(g_wait_timeouts, &z, sizeof(z));
+  return v;
+}
 
 bool m1_supported(int64_t M, int64_t K, int64_t N, int group) {
   // two words per lane: N / 16 even; kD-row blocks never straddle a group

@@ -8,14 +8,17 @@
 namespace grinqh {
 
 // Fused all-reduce over the tensor-parallel ranks' peer buffers (grinqh_gemv_allreduce).
-// Buffer of a rank: [0] epoch of its last completed launch; at kArParts the partial
-// sums [2 (epoch parity)][world][n_cap], each a 64-bit word {fp32 bits, epoch} written
-// by the rank that computed it (the epoch in the word tells the reader it is current).
+// Buffer of a rank: word 0 = epoch of its last completed launch, word 1 = count of this
+// launch's CTAs that have finished (the last one publishes the epoch and clears the
+// count); at kArParts the partial sums [2 (epoch parity)][world][n_cap], each a 64-bit
+// word {fp32 bits, epoch} written by the rank that computed it (the epoch in the word
+// tells the reader it is current).
 constexpr int kArMaxRanks = 8;
 constexpr size_t kArParts = 256;
 struct M1AllReduce {
   unsigned char* buf[kArMaxRanks];  // every rank's buffer as mapped in this process
   int rank, world, n_cap;
+  unsigned long long wait_ns;       // a peer's partial not seen after this long: give up
 };
 
 struct M1Args {
@@ -51,6 +54,9 @@ M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
 // that the column slices alone fill the GPU)
 inline bool m1_plan_fits(const M1Plan& p) { return p.smem_bytes <= 227u * 1024u; }
 int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t st, bool allreduce = false);
+// Reads and clears the count of fused all-reduce waits that gave up (this file's copy
+// of the bounded-wait counter).
+unsigned take_m1_timeouts();
 inline size_t m1_allreduce_buffer_bytes(int world, int64_t n_cap) {
   return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(uint64_t);
 }

@@ -264,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     }
     if (split) {
       // Split-K fix-up, shared by the tile's splits: each one arrives on the tile's
-      // ticket, waits until every split has written its sums (the planner keeps the
-      // grid within one wave, so they are all resident; the wait is bounded), then adds
+      // ticket, waits until every split has written its sums (the grid is launched
+      // cooperatively, so they are all resident; the wait is bounded), then adds
       // its share of the tile's rows over the splits in split order and stores them.
       // A second count on the same ticket lets the last one reset it.
       constexpr int kEpiThreads = 32 * kEpiWarps;
@@ -372,7 +372,26 @@ int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN), (unsigned)a.splits);
-  kern<<<grid, kThreads, kSmemBytes, st>>>(tmap_x, tmap_w, a);
+  if (a.splits <= 1) {
+    kern<<<grid, kThreads, kSmemBytes, st>>>(tmap_x, tmap_w, a);
+    return check_launch("gemm_bf16");
+  }
+  // The splits of a tile wait for one another in the fix-up, so every CTA of the grid
+  // must be resident at once. A cooperative launch guarantees that (the planner keeps
+  // the grid within one CTA per SM), also when kernels of other streams hold SMs; a
+  // grid that could not be co-resident fails to launch instead of waiting.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e2 = cudaLaunchKernelEx(&cfg, kern, tmap_x, tmap_w, a);
+  if (e2 != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "gemm_bf16 (split-K) launch: %s", cudaGetErrorString(e2));
   return check_launch("gemm_bf16");
 }
 

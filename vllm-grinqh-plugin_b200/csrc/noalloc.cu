@@ -32,7 +32,10 @@ size_t round256(size_t v) { return (v + 255) / 256 * 256; }
 
 // Device address of the scratch array on the current device. The array's name in
 // host code is only a host-side handle, so the address must be looked up once per
-// device with that device current; the lookup happens on the first call there.
+// device with that device current; the lookup happens on the first call there. The
+// address belongs to the device's primary context: it is not valid after that context
+// is destroyed (cudaDeviceReset), so a process that resets a device must not call
+// grinqh_gemv_noalloc on it again.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

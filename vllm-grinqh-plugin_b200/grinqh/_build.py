@@ -49,18 +49,35 @@ def _run(cmd, verbose):
     subprocess.run(cmd, check=True)
 
 
+OBJ_DIR = os.path.join(PLUGIN_DIR, "_build")
+
+
 def build_lib(force: bool = False, verbose: bool = True) -> str:
+    """Each .cu compiles to its own object (in parallel; a source recompiles when it or
+    any header is newer than its object), then nvcc links the shared library."""
+    from concurrent.futures import ThreadPoolExecutor
+
     cu = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    deps = cu + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
-    if force or _stale(LIB, deps):
-        nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
-        cmd = [nvcc, *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-               f"-I{INCLUDE}", f"-I{CSRC}", "--expt-relaxed-constexpr", "-diag-suppress", "177",
-               *cu, "-o", LIB + ".tmp"]
-        # no -lcuda: the library must load on hosts without a driver (CPU CI);
-        # cudart is linked statically by nvcc and finds the driver at first use.
-        _run(cmd, verbose)
-        os.replace(LIB + ".tmp", LIB)
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    if not (force or _stale(LIB, cu + headers)):
+        return LIB
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
+    flags = [*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}",
+             "--expt-relaxed-constexpr", "-diag-suppress", "177"]
+    objs, jobs = [], []
+    for src in cu:
+        obj = os.path.join(OBJ_DIR, os.path.basename(src)[:-3] + ".o")
+        objs.append(obj)
+        if force or _stale(obj, [src] + headers):
+            jobs.append([nvcc, *flags, "-c", src, "-o", obj])
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(_run, j, verbose) for j in jobs]:
+            f.result()
+    # no -lcuda: the library must load on hosts without a driver (CPU CI);
+    # cudart is linked statically by nvcc and finds the driver at first use.
+    _run([nvcc, *ARCH_FLAGS, "-shared", *objs, "-o", LIB + ".tmp"], verbose)
+    os.replace(LIB + ".tmp", LIB)
     return LIB
 
 

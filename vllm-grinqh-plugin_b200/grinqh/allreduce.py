@@ -96,20 +96,33 @@ _TP_PEERS: Dict[int, PeerBuffers] = {}
 
 
 def tp_peers(device: torch.device, n_cap: int) -> PeerBuffers:
+    """The device's peer buffers, grown (collectively: every rank makes the same calls)
+    when a layer is wider than they hold. The replaced buffers are closed, so growth
+    must not happen while a captured CUDA graph still uses them: it is refused during
+    capture (the first forward, before any capture, sizes them for the model)."""
     from vllm.distributed import get_tp_group
     key = torch.device(device).index or 0
     p = _TP_PEERS.get(key)
     if p is None or p.n_cap < n_cap:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("GRINQH fused all-reduce: peer buffers must be sized before CUDA-graph capture "
+                               f"(need {n_cap} columns)")
+        if p is not None:
+            p.close()
         p = PeerBuffers(get_tp_group().cpu_group, max(int(n_cap), 8192), device)
         _TP_PEERS[key] = p
     return p
 
 
-def fused_row_supported(x: torch.Tensor, weight_packed: torch.Tensor, original_n: int, group_size: int) -> bool:
-    """The fused kernel takes one row of x and the single-row GEMV's shapes."""
+def fused_row_supported(x: torch.Tensor, weight_packed: torch.Tensor, weight_scale: torch.Tensor,
+                        original_n: int, group_size: int) -> bool:
+    """The fused kernel takes one row of x, the single-row GEMV's shapes, 8-byte aligned
+    packed weights and 4-byte aligned scales (grinqh_gemv_allreduce refuses the rest;
+    a shape whose launch plan does not fit is refused by the call itself)."""
     n = 4 * original_n
     return (x.numel() == weight_packed.shape[0] and n % 32 == 0 and group_size % 4 == 0
-            and weight_packed.shape[0] % group_size == 0)
+            and weight_packed.shape[0] % group_size == 0 and weight_packed.data_ptr() % 8 == 0
+            and weight_scale.data_ptr() % 4 == 0)
 
 
 @torch.library.custom_op("grinqh::row_parallel_linear", mutates_args=())
@@ -121,10 +134,14 @@ def row_parallel_linear(x: torch.Tensor, weight_packed: torch.Tensor, weight_sca
     followed by vLLM's all-reduce (RowParallelLinear.forward), bias on rank 0 only.
     Opaque to the compiler, so the branch on the row count is taken at run time."""
     from vllm.distributed import get_tensor_model_parallel_rank, tensor_model_parallel_all_reduce
-    if fused_row_supported(x, weight_packed, original_n, group_size):
+    if fused_row_supported(x, weight_packed, weight_scale, original_n, group_size):
         peers = tp_peers(x.device, 4 * original_n)
-        return gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds,
-                              peers)
+        try:
+            return gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n,
+                                  thresholds, peers)
+        except RuntimeError as e:  # refused before launch (every rank refuses alike): unfused path
+            if "not supported by the GEMV" not in str(e):
+                raise
     rank_bias = bias if get_tensor_model_parallel_rank() == 0 else None
     y = torch.ops.grinqh.gemm_or_gemv(x, weight_packed, weight_scale, rank_bias, max_bits, group_size, original_n,
                                       thresholds, False)
