@@ -232,11 +232,13 @@ def test_llama_shapes_graded_m1(K, N, b, m1_kernel):
     assert_parity(f32(y)[0], O.to_f32(O.round_to_dtype(ref, "bf16"), "bf16"))
 
 
-@pytest.mark.parametrize("K,N", [(512, 4128), (384, 4112), (1024, 96), (256, 1056)])
+@pytest.mark.parametrize("K,N", [(512, 4128), (384, 4112), (1024, 96), (256, 1056), (512, 4160), (1024, 64),
+                                 (384, 1088), (4096, 9216)])
 @pytest.mark.parametrize("b", [8, 6, 2])
 def test_ragged_widths_graded_m1(K, N, b, m1_kernel):
-    """Widths that leave a partial 1024-column slice (N = 4128, 1056), fall back to the
-    generic kernel (N / 16 odd: 4112) or fill less than one slice (96)."""
+    """Widths the single-row kernel slices unevenly: a partial last 1024-column slice
+    (N = 4128, 1056, 4160, 1088, 9216), less than one slice (96, 64); N / 16 odd (4112)
+    runs the generic kernel."""
     from grinqh.kernel import grinqh_gemm_or_gemv
     from grinqh.utils import pack_codes
     rng = np.random.default_rng(K * 7 + N + b)

@@ -19,9 +19,18 @@
 #include <utility>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "grinqh_b200.h"
 
 namespace {
+
+// An NVTX range around each op call, so that profilers (nsys, ncu --nvtx) attribute the
+// kernels to the quantized linear; without a tool attached the calls do nothing.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
 
 int dtype_code(const at::Tensor& t, const char* name) {
   if (t.scalar_type() == at::kBFloat16) return GRINQH_BF16;
@@ -93,6 +102,7 @@ int env_mode_for_rows() {
 at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
                       const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
                       int64_t original_n, at::ArrayRef<double> thresholds, int mode) {
+  const NvtxRange range("grinqh::linear");
   check_cuda(x, "x");
   check_cuda(weight_packed, "weight_packed");
   check_cuda(weight_scale, "weight_scale");
@@ -148,6 +158,7 @@ at::Tensor gemv_allreduce(const at::Tensor& x, const at::Tensor& weight_packed, 
                           const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
                           int64_t original_n, at::ArrayRef<double> thresholds, int64_t rank, int64_t world,
                           at::ArrayRef<int64_t> buffers, int64_t n_cap) {
+  const NvtxRange range("grinqh::gemv_allreduce");
   check_cuda(x, "x");
   check_cuda(weight_packed, "weight_packed");
   check_cuda(weight_scale, "weight_scale");
