@@ -434,3 +434,41 @@ def test_dense_two_pass_gemm(M, K, N, dtype, b):
     y2 = grinqh_gemm_or_gemv(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128,
                              N // 4, [0.0] * 4)
     assert torch.equal(y, y2), "two-pass GEMM is not deterministic"
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 1024, 512), (300, 512, 1056), (256, 384, 4096)])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("b", [8, 6, 4, 2])
+@pytest.mark.parametrize("q", ["spread", "non_monotone"])
+def test_graded_prefill_tensor_cores(M, K, N, dtype, b, q):
+    """MODE_GRADED with 128 rows or more runs the tensor-core graded prefill: one fp16 GEMM
+    over the zone-masked activations and the zone weight operands (bias folded in). Against
+    the oracle's per-token grading (grinqh/kernel.py:100-158 applied row by row), with a
+    row tail (300 rows), a partial column tile (1056), non-monotone thresholds (masks
+    with gaps), bias, and a block of rows whose activations are all zero (skipped steps)."""
+    from grinqh.kernel import MODE_GRADED, grinqh_linear
+    from grinqh.utils import pack_codes
+    rng = np.random.default_rng(M + K + N + b + len(q))
+    lim = 1 << (b - 1)
+    codes = rng.integers(-lim, lim, size=(K, N)).astype(np.int8)
+    s32 = (rng.random((K // 128, N)) * 0.02 + 0.001).astype(np.float32)
+    s_store = O.round_to_dtype(s32, dtype)
+    x, _ = O.make_activations(rng, M, K, dist="t3")
+    x[: min(M, 256) // 2, : K // 2] = 0.0  # a zero block: its steps have no active value
+    xs = O.round_to_dtype(x, dtype)
+    x32 = O.to_f32(xs, dtype)
+    ax = np.abs(x32[np.abs(x32) > 0])
+    qs = [0.2, 0.4, 0.6, 0.8] if q == "spread" else [0.5, 0.1, 0.9, 0.3]
+    th = O.quantile_thresholds(ax, qs)
+    bias = O.round_to_dtype(rng.standard_normal(N).astype(np.float32), dtype)
+    w = pack_codes(torch.from_numpy(codes).cuda(), b)
+    y = grinqh_linear(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128, N // 4, th,
+                      MODE_GRADED)
+    # the op's result: the graded rows rounded to dtype, then the bias added in dtype
+    # (grinqh/kernel.py:706-708), as oracle.gemm_or_gemv(graded_prefill=True) computes it
+    yr = O.to_f32(O.round_to_dtype(O.graded_rows(x32, codes, O.to_f32(s_store, dtype), th, b, 128), dtype), dtype)
+    ref = O.to_f32(O.round_to_dtype(yr.astype(np.float64) + O.to_f32(bias, dtype)[None, :], dtype), dtype)
+    assert_parity(f32(y), ref)
+    y2 = grinqh_linear(dev_act(xs, dtype), w, dev_act(s_store, dtype), dev_act(bias, dtype), b, 128, N // 4, th,
+                       MODE_GRADED)
+    assert torch.equal(y, y2), "graded prefill is not deterministic"

@@ -164,6 +164,13 @@ static bool use_bf16_gemm(int kmode, int64_t M, int64_t K, int64_t N, int sms) {
   return M >= 512 || fused_ctas < sms / 2;
 }
 
+// Rows graded one by one (GRINQH_MODE_GRADED) take the tensor-core graded prefill from
+// this many rows on (its per-call preparation of the zone operands costs about one pass
+// over the weights); fewer rows run the generic kernel.
+constexpr int64_t kGradedTcMinRows = 128;
+
+static bool use_graded_gemm(int kmode, int64_t M) { return kmode == kModeGraded && M >= kGradedTcMinRows; }
+
 static bool use_skinny(int kmode, int64_t M, int64_t K, int64_t N, int group) {
   return kmode == kModeDense && M >= 2 && M <= kSkinnyMaxRows && skinny_supported(M, K, N, group);
 }
@@ -230,6 +237,10 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   // an activation or output view that the tensor-core kernels cannot take (alignment)
   // runs the generic kernel, and this query does not see the pointers: cover both
   const size_t generic = workspace_for(plan_decode(M, K, N, km, sms));
+  if (use_graded_gemm(km, M) && K % 64 == 0 && N % 32 == 0) {
+    const size_t a = graded_gemm_workspace(M, K, N, max_bits / 2, sms);
+    return a > generic ? a : generic;
+  }
   if (use_bf16_gemm(km, M, K, N, sms)) {
     // the dtype(w * s) buffer sits after the ticket region, then the split-K sums
     const int splits = bf16_gemm_splits(M, K, N, sms);
@@ -304,6 +315,24 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
       GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
                                       &g.counters));
     return launch_m1(g, plan, dtype, max_bits / 2, stream);
+  }
+
+  if (use_graded_gemm(km, M) && graded_gemm_supported(M, K, N, group, x, w, s, y)) {
+    const size_t need = graded_gemm_workspace(M, K, N, max_bits / 2, sms);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(aligned(workspace, 256), "workspace must be 256-byte aligned");
+    Bf16GemmArgs g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.M = (int)M;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    return launch_graded_gemm(g, thresholds, workspace, dtype, max_bits / 2, sms, stream);
   }
 
   if (use_skinny(km, M, K, N, group) && skinny_pointers_ok(x, w, s)) {

@@ -129,7 +129,8 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-template <typename T>
+// TI: operand type of x and W (bf16 / fp16); TO: output type (the activation dtype)
+template <typename TI, typename TO>
 __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                   const __grid_constant__ CUtensorMap tmap_w,
                                                                   const Bf16GemmArgs a) {
@@ -152,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
   const int per = (nk_all + a.splits - 1) / a.splits;
   const int q_begin = blockIdx.z * per;
   const int nk = max(0, min(nk_all, q_begin + per) - q_begin);
+  const unsigned* active = a.active;
+  const size_t act_base = (size_t)blockIdx.x * nk_all + q_begin;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -172,23 +175,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
       prefetch_tmap(&tmap_w);
+      int qa = 0;  // K steps loaded so far (steps without an active row are skipped)
       for (int q = 0; q < nk; ++q) {
-        const int s = q % STAGES;
-        if (q >= STAGES) mbar_wait(&empty[s], ((q / STAGES) - 1) & 1);
+        if (active && active[act_base + q] == 0u) continue;
+        const int s = qa % STAGES;
+        if (qa >= STAGES) mbar_wait(&empty[s], ((qa / STAGES) - 1) & 1);
         mbar_arrive_expect_tx(&full[s], kStageA + kStageB);
         tma_load_2d(sA + s * kStageA, &tmap_x, (q_begin + q) * BK, m0, &full[s]);
 #pragma unroll
         for (int b = 0; b < BN / 64; ++b)
           tma_load_2d(sB + s * kStageB + b * kBoxB, &tmap_w, n0 + 64 * b, (q_begin + q) * BK, &full[s]);
+        ++qa;
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(1, Fmt<T>::v, Fmt<T>::v, 0, 1, BN, 128);
+      constexpr uint32_t idesc = instr_desc(1, Fmt<TI>::v, Fmt<TI>::v, 0, 1, BN, 128);
+      int qa = 0;
       for (int q = 0; q < nk; ++q) {
-        const int s = q % STAGES;
-        mbar_wait(&full[s], (q / STAGES) & 1);
+        if (active && active[act_base + q] == 0u) continue;
+        const int s = qa % STAGES;
+        mbar_wait(&full[s], (qa / STAGES) & 1);
         tc_fence_after();
         const uint32_t a_base = smem_u32(sA + s * kStageA);
         const uint32_t b_base = smem_u32(sB + s * kStageB);
@@ -198,10 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint64_t adesc = smem_desc(a_base + h * 128 * 128 + kk * 32, 16, kSboA, 2);
-            mma_f16_ss(tmem + h * BN, adesc, bdesc, idesc, (q > 0 || kk > 0) ? 1u : 0u);
+            mma_f16_ss(tmem + h * BN, adesc, bdesc, idesc, (qa > 0 || kk > 0) ? 1u : 0u);
           }
         }
         mma_commit(&empty[s]);
+        ++qa;
       }
       mma_commit(acc_full);
     }
@@ -214,18 +223,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int m = m0 + half * 128 + quarter * 32 + lane;
-    T* y = static_cast<T*>(a.y);
-    const T* bias = static_cast<const T*>(a.bias);
+    TO* y = static_cast<TO*>(a.y);
+    const TO* bias = static_cast<const TO*>(a.bias);
+    const float osc = a.out_scale ? *a.out_scale : 1.0f;
+    // with skipped K steps, whether this split's accumulator was written at all
+    bool any_mma = nk > 0;
+    if (active) {
+      bool any = false;
+      for (int q = lane; q < nk; q += 32) any |= active[act_base + q] != 0u;
+      any_mma = __any_sync(0xFFFFFFFFu, any);
+    }
     // 8 columns (16 bytes of y) of row mm at a time: cast, bias, one 16-byte store
     auto store8 = [&](int mm, int n, const float* v) {
       uint32_t o[4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        T lo = Act<T>::from_f(v[2 * t]);
-        T hi = Act<T>::from_f(v[2 * t + 1]);
+        TO lo = Act<TO>::from_f(v[2 * t] * osc);
+        TO hi = Act<TO>::from_f(v[2 * t + 1] * osc);
         if (bias) {
-          lo = Act<T>::from_f(Act<T>::to_f(lo) + Act<T>::to_f(bias[n + 2 * t]));
-          hi = Act<T>::from_f(Act<T>::to_f(hi) + Act<T>::to_f(bias[n + 2 * t + 1]));
+          lo = Act<TO>::from_f(Act<TO>::to_f(lo) + Act<TO>::to_f(bias[n + 2 * t]));
+          hi = Act<TO>::from_f(Act<TO>::to_f(hi) + Act<TO>::to_f(bias[n + 2 * t + 1]));
         }
         o[t] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
       }
@@ -235,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
 #pragma unroll 1
     for (int cc = 0; cc < BN / 32; ++cc) {
       uint32_t r[32];
-      if (nk > 0) {
+      if (any_mma) {
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + half * BN + cc * 32, r);
         tmem_ld_wait();
       } else {
@@ -333,17 +350,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int NZ, typename T>
-int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
-  // pass 1
-  {
-    const int pairs = a.N / 32;
-    const dim3 grid((unsigned)((pairs + 127) / 128), (unsigned)((a.K + kDqRows - 1) / kDqRows));
-    dequant_kernel<NZ, T><<<grid, 128, 0, st>>>(a.w, static_cast<const T*>(a.s), static_cast<T*>(a.wbuf), a.K, a.N,
-                                                a.group);
-    GRINQH_RETURN_IF(check_launch("dequant"));
-  }
-  // pass 2
+// y = x @ W on the tensor cores: x [M, a.K] and W = a.wbuf [a.K, N] of operand type TI,
+// y of type TO (a.splits K splits, a.active / a.out_scale as set).
+template <typename TI, typename TO>
+int launch_gemm_pass(const Bf16GemmArgs& a, cudaStream_t st) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cuuint32_t estride[2] = {1, 1};
@@ -352,7 +362,7 @@ int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
     const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
     const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
     const cuuint32_t box[2] = {BK, BM};
-    const CUresult r = enc(&tmap_x, Fmt<T>::tma, 2, const_cast<void*>(a.x), gdim, gstride, box, estride,
+    const CUresult r = enc(&tmap_x, Fmt<TI>::tma, 2, const_cast<void*>(a.x), gdim, gstride, box, estride,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed (%d)", (int)r);
@@ -363,12 +373,12 @@ int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
     const cuuint64_t gdim[2] = {(cuuint64_t)a.N, (cuuint64_t)a.K};
     const cuuint64_t gstride[1] = {(cuuint64_t)a.N * 2};
     const cuuint32_t box[2] = {64, BK};
-    const CUresult r = enc(&tmap_w, Fmt<T>::tma, 2, a.wbuf, gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const CUresult r = enc(&tmap_w, Fmt<TI>::tma, 2, a.wbuf, gdim, gstride, box, estride,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed (%d)", (int)r);
   }
-  auto kern = gemm_bf16_kernel<T>;
+  auto kern = gemm_bf16_kernel<TI, TO>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const dim3 grid((unsigned)((a.M + BM - 1) / BM), (unsigned)((a.N + BN - 1) / BN), (unsigned)a.splits);
@@ -393,6 +403,20 @@ int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
   const cudaError_t e2 = cudaLaunchKernelEx(&cfg, kern, tmap_x, tmap_w, a);
   if (e2 != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "gemm_bf16 (split-K) launch: %s", cudaGetErrorString(e2));
   return check_launch("gemm_bf16");
+}
+
+template <int NZ, typename T>
+int launch_t(const Bf16GemmArgs& a, cudaStream_t st) {
+  // pass 1
+  {
+    const int pairs = a.N / 32;
+    const dim3 grid((unsigned)((pairs + 127) / 128), (unsigned)((a.K + kDqRows - 1) / kDqRows));
+    dequant_kernel<NZ, T><<<grid, 128, 0, st>>>(a.w, static_cast<const T*>(a.s), static_cast<T*>(a.wbuf), a.K, a.N,
+                                                a.group);
+    GRINQH_RETURN_IF(check_launch("dequant"));
+  }
+  // pass 2
+  return launch_gemm_pass<T, T>(a, st);
 }
 
 }  // namespace
@@ -455,6 +479,259 @@ int launch_bf16_gemm(const Bf16GemmArgs& a, int dtype, int nz, cudaStream_t st) 
     case 2: return launch_t<2, __half>(a, st);
     case 3: return launch_t<3, __half>(a, st);
     default: return launch_t<4, __half>(a, st);
+  }
+}
+
+
+// ---------------------------------------------------------------- graded prefill
+// Every row graded by its own activations (the reference's one-row GEMV applied row by
+// row, grinqh/kernel.py:100-158), for many rows, on the tensor cores. For element
+// (m, k) with active zones Z, the reference adds s * x * (w_Z + bias(Z)) with
+// w_Z = int8(byte & zone bits) >> shift and bias(Z) = sum_{z in Z} Delta_z. Both are
+// sums over the active zones: w_Z = sum_{z in Z} D_z / 2^shift with D_0 the signed top
+// bit pair * 64 and D_z = (bit pair z) * 4^(3-z), so
+//   y[m, n] = sum_z sum_k A_z[m, k] B_z[k, n],
+//   A_z[m, k] = x[m, k] if |x[m, k]| > t_z else 0,
+//   B_z[k, n] = s[k / g, n] * (D_z + Delta_z 2^shift) / 2^shift,
+// one GEMM over K' = (b/2) K. (D_z + Delta_z 2^shift) is 2^p times an odd number below 4
+// (or 0), so B_z has at most 10 significant bits: exact in fp16 (not in bf16). Both
+// operands are scaled by powers of two into fp16's range (x's largest |x| near 2^14, the
+// largest |B| below 2^15) and the sums scaled back in the GEMM's epilogue.
+namespace {
+
+constexpr size_t kGradedHead = 16 << 10;  // split-K tickets; then 3 words of scaling; then the step flags
+
+__device__ __forceinline__ void atomic_max_pos(unsigned* p, float v) {
+  // non-negative floats order like their bit patterns
+  atomicMax(p, __float_as_uint(v));
+}
+
+// scal[0] = bits of max |x| (finite), scal[1] = bits of max |s| (finite)
+template <typename T>
+__global__ void __launch_bounds__(256) graded_max_kernel(const T* __restrict__ x, size_t nx, const T* __restrict__ s,
+                                                         size_t ns, unsigned* scal) {
+  float mx = 0.f, ms = 0.f;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nx; i += stride) {
+    const float v = fabsf(Act<T>::to_f(x[i]));
+    if (v < INFINITY) mx = fmaxf(mx, v);
+  }
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns; i += stride) {
+    const float v = fabsf(Act<T>::to_f(s[i]));
+    if (v < INFINITY) ms = fmaxf(ms, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    ms = fmaxf(ms, __shfl_xor_sync(0xFFFFFFFFu, ms, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomic_max_pos(scal, mx);
+    atomic_max_pos(scal + 1, ms);
+  }
+}
+
+__device__ __forceinline__ int exp_for(unsigned bits, int top) {  // 2^e puts the max below 2^top
+  const float m = __uint_as_float(bits);
+  if (!(m > 0.f) || !(m < INFINITY)) return 0;
+  return max(-60, min(60, ilogbf(m) - (top - 1)));
+}
+
+// A_z = fp16(x * 2^-eA) where |x| > t_z, else 0, for the zones z < NZ: row m of A' holds
+// [A_0 | A_1 | ...] (NZ K columns). flags[(m / 256) * nk' + k' / 64] = 1 where a 64-deep
+// step of a 256-row tile has a non-zero value. Thread: 8 consecutive k of one row.
+template <int NZ, typename T>
+__global__ void __launch_bounds__(256) graded_a_kernel(const T* __restrict__ x, int M, int K, float t0, float t1,
+                                                       float t2, float t3, unsigned* scal, __half* __restrict__ A,
+                                                       unsigned* flags) {
+  const int per_row = K / 8;
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int eA = exp_for(scal[0], 14);
+  if (idx == 0) {  // the GEMM's output scale 2^(eA + eB)
+    const int eB = exp_for(scal[1], 8);  // |B| <= 128 max|s| < 2^15
+    reinterpret_cast<float*>(scal)[2] = ldexpf(1.0f, eA + eB);
+  }
+  if (idx >= (size_t)M * per_row) return;
+  const int m = (int)(idx / per_row), k = (int)(idx % per_row) * 8;
+  const float down = ldexpf(1.0f, -eA);
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K + k));
+  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  float xf[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint16_t bits = (uint16_t)(wv[e >> 1] >> (16 * (e & 1)));
+    xf[e] = Act<T>::to_f(*reinterpret_cast<const T*>(&bits));
+  }
+  const float th[4] = {t0, t1, t2, t3};
+  const int nk = NZ * K / 64;
+#pragma unroll
+  for (int z = 0; z < NZ; ++z) {
+    uint32_t o[4];
+    bool any = false;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      // fp32 |x| > t_z, strict; NaN is never active (kernel.py:100-116)
+      const float a0 = fabsf(xf[e]) > th[z] ? xf[e] * down : 0.f;
+      const float a1 = fabsf(xf[e + 1]) > th[z] ? xf[e + 1] * down : 0.f;
+      any |= (a0 != 0.f) | (a1 != 0.f);
+      __half2 h = __floats2half2_rn(a0, a1);
+      o[e / 2] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    const size_t col = (size_t)z * K + k;
+    *reinterpret_cast<uint4*>(A + (size_t)m * NZ * K + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (any) flags[(size_t)(m / 256) * nk + col / 64] = 1u;
+  }
+}
+
+// B_z[k, n] = fp16(s[k / g, n] * (D_z + Delta_z 2^shift) / 2^shift * 2^-eB) for z < NZ,
+// rows z K + k of B' [NZ K, N] in the original column order. Thread: the packed words
+// 2p, 2p + 1 of kDqRows consecutive rows of one scale group (as dequant_kernel).
+template <int NZ, typename T>
+__global__ void __launch_bounds__(128) graded_b_kernel(const uint32_t* __restrict__ w, const T* __restrict__ s,
+                                                       const unsigned* scal, __half* __restrict__ B, int K, int N,
+                                                       int group) {
+  constexpr int kShift = 8 - 2 * NZ;
+  const int n16 = N >> 4;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= (n16 >> 1)) return;
+  const int j = 2 * p;
+  const int k0 = blockIdx.y * kDqRows;
+  if (k0 >= K) return;
+  const int k1 = min(K, k0 + kDqRows);
+  const size_t row_words = (size_t)NZ * n16;
+  // per zone: (D_z + Delta_z 2^shift) = coef_z(field) * 2^p_z, taken from the byte below;
+  // Delta_z = B_z - B_{z-1}, B_z = 2^(b-1) >> (2z + 2) (kernel.py:73-82)
+  int delta[4];
+  {
+    const int base = 1 << (2 * NZ - 1);
+    int prev = 0;
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int bz = base >> (2 * z + 2);
+      delta[z] = bz - prev;
+      prev = bz;
+    }
+  }
+  const float post = ldexpf(1.0f, -kShift - exp_for(scal[1], 8));  // 2^-shift * 2^-eB
+  float2 sc[16];
+  {
+    const uint32_t* sp = reinterpret_cast<const uint32_t*>(s + (size_t)(k0 / group) * N + j);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint32_t bits = __ldg(sp + (size_t)c * (n16 >> 1));
+      if constexpr (Act<T>::kBf16) {
+        sc[c] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bits));
+      } else {
+        sc[c] = __half22float2(*reinterpret_cast<const __half2*>(&bits));
+      }
+      sc[c].x *= post;  // exact: a power of two
+      sc[c].y *= post;
+    }
+  }
+  const uint32_t* wp = w + (size_t)k0 * row_words + j;
+  for (int k = k0; k < k1; ++k, wp += row_words) {
+    uint2 P[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z)
+      P[z] = z < NZ ? __ldcs(reinterpret_cast<const uint2*>(wp + (size_t)z * n16)) : make_uint2(0u, 0u);
+    uint32_t qa[4], qb[4];
+    // plain merge (no sign flip): the bytes are the shifted two's-complement codes
+    merge_planes(P[0].x, P[1].x, P[2].x, P[3].x, qa);
+    merge_planes(P[0].y, P[1].y, P[2].y, P[3].y, qb);
+#pragma unroll
+    for (int z = 0; z < NZ; ++z) {
+      __half* op = B + ((size_t)z * K + k) * N + j;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int L = 0; L < 4; ++L) {
+          const int c = 4 * i + L;
+          const int ba = (int)((qa[i] >> (8 * L)) & 0xFFu), bb = (int)((qb[i] >> (8 * L)) & 0xFFu);
+          // D_z: the signed top bit pair * 64 for z = 0, bit pair z * 4^(3-z) otherwise
+          const int da = z == 0 ? ((int)(int8_t)ba >> 6) * 64 : ((ba >> (6 - 2 * z)) & 3) << (6 - 2 * z);
+          const int db = z == 0 ? ((int)(int8_t)bb >> 6) * 64 : ((bb >> (6 - 2 * z)) & 3) << (6 - 2 * z);
+          const int ea = da + (delta[z] << kShift), eb = db + (delta[z] << kShift);
+          __half2 h = __floats2half2_rn((float)ea * sc[c].x, (float)eb * sc[c].y);
+          *reinterpret_cast<__half2*>(op + (size_t)c * n16) = h;
+        }
+    }
+  }
+}
+
+template <int NZ, typename T>
+int launch_graded_t(const Bf16GemmArgs& a, const float* th, void* ws, int sms, cudaStream_t st) {
+  char* base = static_cast<char*>(ws);
+  const int nkp = NZ * a.K / BK;  // 64-deep steps of K'
+  const int mtiles = (a.M + BM - 1) / BM;
+  unsigned* counters = reinterpret_cast<unsigned*>(base);
+  unsigned* scal = reinterpret_cast<unsigned*>(base + kGradedHead);
+  unsigned* flags = scal + 4;
+  const size_t head = kGradedHead + 16 + (size_t)mtiles * nkp * 4;
+  __half* A = reinterpret_cast<__half*>(base + (head + 255) / 256 * 256);
+  const size_t a_bytes = (size_t)a.M * NZ * a.K * 2;
+  __half* Bw = reinterpret_cast<__half*>(reinterpret_cast<char*>(A) + (a_bytes + 255) / 256 * 256);
+  const size_t b_bytes = (size_t)NZ * a.K * a.N * 2;
+  float* slots = reinterpret_cast<float*>(reinterpret_cast<char*>(Bw) + (b_bytes + 255) / 256 * 256);
+  cudaError_t e = cudaMemsetAsync(base, 0, head, st);  // tickets, scaling, flags
+  if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  graded_max_kernel<T><<<sms * 4, 256, 0, st>>>(static_cast<const T*>(a.x), (size_t)a.M * a.K,
+                                                  static_cast<const T*>(a.s), (size_t)(a.K / a.group) * a.N, scal);
+  GRINQH_RETURN_IF(check_launch("graded max"));
+  {
+    const size_t threads = (size_t)a.M * (a.K / 8);
+    graded_a_kernel<NZ, T><<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+        static_cast<const T*>(a.x), a.M, a.K, th[0], th[1], th[2], th[3], scal, A, flags);
+    GRINQH_RETURN_IF(check_launch("graded A"));
+  }
+  {
+    const int pairs = a.N / 32;
+    const dim3 grid((unsigned)((pairs + 127) / 128), (unsigned)((a.K + kDqRows - 1) / kDqRows));
+    graded_b_kernel<NZ, T><<<grid, 128, 0, st>>>(a.w, static_cast<const T*>(a.s), scal, Bw, a.K, a.N, a.group);
+    GRINQH_RETURN_IF(check_launch("graded B"));
+  }
+  Bf16GemmArgs g = a;
+  g.x = A;
+  g.K = NZ * a.K;
+  g.wbuf = Bw;
+  g.splits = bf16_gemm_splits(a.M, g.K, a.N, sms);
+  g.counters = counters;
+  g.slots = slots;
+  g.active = flags;
+  g.out_scale = reinterpret_cast<const float*>(scal) + 2;
+  return launch_gemm_pass<__half, T>(g, st);
+}
+
+}  // namespace
+
+bool graded_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* w, const void* s,
+                           const void* y) {
+  return bf16_gemm_supported(M, K, N, group, x, w, s, y) && K % 8 == 0 && group % kDqRows == 0;
+}
+
+size_t graded_gemm_workspace(int64_t M, int64_t K, int64_t N, int nz, int sm_count) {
+  const int64_t nkp = nz * K / BK, mtiles = (M + BM - 1) / BM;
+  const size_t head = kGradedHead + 16 + (size_t)mtiles * nkp * 4;
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  const int splits = bf16_gemm_splits(M, nz * K, N, sm_count);
+  return up(head) + up((size_t)M * nz * K * 2) + up((size_t)nz * K * N * 2) +
+         up(bf16_gemm_slot_bytes(M, N, splits));
+}
+
+int launch_graded_gemm(const Bf16GemmArgs& a, const float* th, void* ws, int dtype, int nz, int sms,
+                       cudaStream_t st) {
+  if (dtype == GRINQH_BF16) {
+    switch (nz) {
+      case 1: return launch_graded_t<1, __nv_bfloat16>(a, th, ws, sms, st);
+      case 2: return launch_graded_t<2, __nv_bfloat16>(a, th, ws, sms, st);
+      case 3: return launch_graded_t<3, __nv_bfloat16>(a, th, ws, sms, st);
+      default: return launch_graded_t<4, __nv_bfloat16>(a, th, ws, sms, st);
+    }
+  }
+  switch (nz) {
+    case 1: return launch_graded_t<1, __half>(a, th, ws, sms, st);
+    case 2: return launch_graded_t<2, __half>(a, th, ws, sms, st);
+    case 3: return launch_graded_t<3, __half>(a, th, ws, sms, st);
+    default: return launch_graded_t<4, __half>(a, th, ws, sms, st);
   }
 }
 

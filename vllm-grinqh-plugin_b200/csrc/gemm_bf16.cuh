@@ -18,7 +18,22 @@ struct Bf16GemmArgs {
   float* slots;         // [splits, M, N] fp32 split-K sums (splits > 1)
   unsigned* counters;   // [tiles] tickets (splits > 1); zero before the first launch, left zero
   int M, K, N, group, splits;
+  // graded prefill only (null otherwise): per (256-row tile of x, 64-deep K step) a
+  // non-zero word if the step has any non-zero activation (steps without one are
+  // skipped), and a device float the fp32 sums are multiplied by before the cast
+  const unsigned* active;
+  const float* out_scale;
 };
+
+// The opt-in per-token graded prefill (GRINQH_MODE_GRADED, many rows) on the same
+// tensor-core GEMM: y = [x masked by zone 0 | ... | by zone b/2 - 1] @ [B_0; ...], one
+// fp16 GEMM over K' = (b/2) K with B_z = s (D_z + Delta_z 2^shift) / 2^shift, the zone's
+// weight contribution plus its mid-point bias (grinqh/kernel.py:73-158), exact in fp16.
+bool graded_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* w,
+                           const void* s, const void* y);
+size_t graded_gemm_workspace(int64_t M, int64_t K, int64_t N, int nz, int sm_count);
+int launch_graded_gemm(const Bf16GemmArgs& a, const float* thresholds, void* workspace, int dtype, int nz,
+                       int sm_count, cudaStream_t st);
 
 bool bf16_gemm_supported(int64_t M, int64_t K, int64_t N, int group, const void* x, const void* w, const void* s,
                          const void* y);
