@@ -14,6 +14,7 @@
  *                               (grinqh_input_preshuffle utils.py:17-22, << (8-b), pack_triton)
  *   grinqh_unpack_checkpoint <- grinqh/grinqh.py:154-168 weight loader (unpack_from_int32 + narrow + copy)
  *   grinqh_gemv_allreduce    <- grinqh/grinqh.py:236-247 apply + vLLM's row-parallel all-reduce (M = 1)
+ *   grinqh_gemm_allreduce    <- the same for one graded row or 2..64 dense rows (batched decode)
  *   grinqh_unpack            <- grinqh/utils.py:149-177  unpack_pyt, :209-223 unpack_triton
  *   grinqh_grade             <- grinqh/kernel.py:100-116 threshold masks of the graded GEMV
  *   grinqh_gemm_or_gemv      <- grinqh/kernel.py:646-710 torch.ops.grinqh.gemm_or_gemv
@@ -180,37 +181,52 @@ int grinqh_gemv_noalloc(const void *x_dev, int dtype, int64_t K, const uint32_t 
                         const void *weight_scale_dev, const void *bias_dev, int max_bits, int group_size,
                         int64_t N, const float *thresholds, void *y_dev, grinqh_stream_t stream);
 
-/* ---- Row-parallel linear with its all-reduce fused in (tensor parallelism, one row).
- * Replaces, for M = 1, the plugin's apply (grinqh/grinqh.py:236-247) followed by vLLM's
+/* ---- Row-parallel linear with its all-reduce fused in (tensor parallelism).
+ * Replaces the plugin's apply (grinqh/grinqh.py:236-247) followed by vLLM's
  * row-parallel all-reduce of the partial outputs (vllm/model_executor/layers/linear.py,
- * RowParallelLinear.forward): each rank computes the graded GEMV of its K slice and the
- * kernel that does so also sums the ranks' fp32 partials over NVLink (plain 64-bit
- * peer stores of {partial, launch epoch} into every rank's buffer, bounded waits on
- * the epochs) and writes the summed y (+ bias, applied once) on every rank, the same
- * bits on every rank.
- *   - Every rank owns one peer buffer of grinqh_allreduce_buffer_bytes(world, n_cap)
- *     bytes from grinqh_allreduce_buffer_alloc (zeroed); the ranks exchange
- *     grinqh_ipc_get_handle handles (64 bytes) and open each other's with
- *     grinqh_ipc_open_handle; buffers_dev[r] is rank r's buffer as mapped in this
- *     process (buffers_dev[rank] the own one). At most 8 ranks.
+ * RowParallelLinear.forward) for one row (the graded GEMV) and for 2..64 rows (the
+ * dense skinny GEMM, batched decode): each rank computes the product of its K slice,
+ * and the kernel that does so also sums the ranks' fp32 partials over NVLink (plain
+ * 64-bit peer stores of {partial, launch epoch} into every rank's buffer, bounded
+ * waits on the epochs) and writes the summed y (+ bias, applied once) on every rank,
+ * the same bits on every rank.
+ *   - Every rank owns one peer buffer of grinqh_allreduce_buffer_bytes(world, cap)
+ *     bytes from grinqh_allreduce_buffer_alloc (zeroed), cap = the largest M * N a call
+ *     will use; the ranks exchange grinqh_ipc_get_handle handles (64 bytes) and open
+ *     each other's with grinqh_ipc_open_handle; buffers_dev[r] is rank r's buffer as
+ *     mapped in this process (buffers_dev[rank] the own one). At most 8 ranks.
  *   - Every rank must make the same sequence of calls on its buffer (launch epochs are
  *     counted on the device, so calls can be recorded in CUDA graphs). A rank that
  *     never arrives makes the others give up after GRINQH_ALLREDUCE_WAIT_MS
  *     milliseconds (environment, read on every call; default 2000):
  *     grinqh_take_error_flags then reports a non-zero count, y is not valid, and
  *     every rank should call grinqh_take_error_flags before its next launch.
- *   - workspace / mode as for grinqh_gemm_or_gemv with M = 1 (GRINQH_WORKSPACE_ZEROED
- *     honoured); thresholds: 4 host floats. */
-size_t grinqh_allreduce_buffer_bytes(int world, int64_t n_cap);
+ *   - grinqh_gemm_allreduce: mode as for grinqh_gemm_or_gemv (AUTO: one row graded,
+ *     more rows dense; GRINQH_WORKSPACE_ZEROED honoured); shapes the fused kernels do
+ *     not take (graded rows beyond one, dense rows beyond 64, unaligned views) return
+ *     GRINQH_ERR_UNSUPPORTED before anything is launched -- the same answer on every
+ *     rank -- and the caller takes the unfused path. The workspace is
+ *     grinqh_allreduce_workspace_size bytes (it may differ from grinqh_workspace_size:
+ *     the fused grid must be resident at once, which can take fewer K splits).
+ *   - grinqh_gemv_allreduce: the one-row form (x [K], y [N]); mode is 0 or
+ *     GRINQH_WORKSPACE_ZEROED; its workspace is grinqh_workspace_size(1, ...).
+ *   - thresholds: 4 host floats (graded rows; may be NULL for dense rows). */
+size_t grinqh_allreduce_buffer_bytes(int world, int64_t cap);
 int grinqh_allreduce_buffer_alloc(size_t bytes, void **buf_dev);
 int grinqh_allreduce_buffer_free(void *buf_dev);
 int grinqh_ipc_get_handle(const void *buf_dev, unsigned char *handle64);
 int grinqh_ipc_open_handle(const unsigned char *handle64, void **buf_dev);
 int grinqh_ipc_close_handle(void *buf_dev);
+size_t grinqh_allreduce_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int group_size, int mode);
+int grinqh_gemm_allreduce(const void *x_dev, int dtype, int64_t M, int64_t K, const uint32_t *weight_packed_dev,
+                          const void *weight_scale_dev, const void *bias_dev, int max_bits, int group_size,
+                          int64_t N, const float *thresholds, int mode, void *y_dev, void *workspace_dev,
+                          size_t workspace_bytes, int rank, int world, void *const *buffers_dev, int64_t cap,
+                          grinqh_stream_t stream);
 int grinqh_gemv_allreduce(const void *x_dev, int dtype, int64_t K, const uint32_t *weight_packed_dev,
                           const void *weight_scale_dev, const void *bias_dev, int max_bits, int group_size,
                           int64_t N, const float *thresholds, void *y_dev, void *workspace_dev,
-                          size_t workspace_bytes, int rank, int world, void *const *buffers_dev, int64_t n_cap,
+                          size_t workspace_bytes, int rank, int world, void *const *buffers_dev, int64_t cap,
                           int mode, grinqh_stream_t stream);
 
 #ifdef __cplusplus

@@ -1,10 +1,12 @@
-"""Fused row-parallel linear (torch.ops.grinqh.gemv_allreduce) on two GPUs: each rank
-runs the graded GEMV of its K slice, and the same kernel sums the ranks' partials over
-NVLink peer buffers. Checked against the CPU oracle of the unsharded layer, for
-identical bits on both ranks, over many consecutive launches (the device-side epoch
-and the double-buffered partials), under CUDA-graph replay, and timed against the
-unfused GEMV followed by an NCCL all-reduce. Needs two GPUs; skipped otherwise. NVLS
-is off (NCCL_NVLS_ENABLE=0) and the kernel uses plain peer stores only."""
+"""Fused row-parallel linear on two GPUs: each rank runs the graded GEMV of its K slice
+(torch.ops.grinqh.gemv_allreduce, one row) or the dense skinny GEMM of its K slice
+(torch.ops.grinqh.linear_allreduce, 2..64 rows), and the same kernel sums the ranks'
+partials over NVLink peer buffers. Checked against the CPU oracle of the unsharded
+layer, for identical bits on both ranks, over many consecutive launches (the
+device-side epoch and the double-buffered partials, shared by one-row and many-row
+launches), under CUDA-graph replay, and timed against the unfused kernel followed by
+an NCCL all-reduce. Needs two GPUs; skipped otherwise. NVLS is off
+(NCCL_NVLS_ENABLE=0) and the kernels use plain peer stores only."""
 import datetime
 import os
 import socket
@@ -45,7 +47,7 @@ def _worker(rank, world, port, q):
                                 device_id=dev)
         import oracle as O
         import grinqh.kernel  # noqa: F401
-        from grinqh.allreduce import PeerBuffers, gemv_allreduce
+        from grinqh.allreduce import PeerBuffers, gemv_allreduce, linear_allreduce
         from grinqh.utils import pack_codes
 
         lines, ok = [], True
@@ -59,7 +61,7 @@ def _worker(rank, world, port, q):
             dist.all_reduce(v, op=dist.ReduceOp.MIN)
             return bool(v.item())
 
-        peers = PeerBuffers(None, n_cap=4096, device=dev)
+        peers = PeerBuffers(None, n_cap=64 * 4096, device=dev)
 
         def bf16(a):
             return O.to_f32(O.round_to_dtype(np.asarray(a, np.float32), "bf16"), "bf16")
@@ -94,6 +96,34 @@ def _worker(rank, world, port, q):
                     lines.append(f"K={K} N={N} it={it}: ranks differ")
             lines.append(f"K={K} N={N} b={b} bias={with_bias}: worst max-rel {worst[0]:.2e} fro {worst[1]:.2e}")
             if not agree(ok):  # stop here on every rank: later phases would only repeat the failure
+                raise RuntimeError("; ".join(lines))
+
+        # 2..64 dense rows (batched decode): the skinny GEMM with the sum fused in,
+        # single-row launches interleaved on the same buffers
+        for (M, K, N, b, with_bias) in ((2, 1024, 512, 8, True), (16, 4096, 4096, 8, False),
+                                        (64, 4096, 4096, 4, True), (64, 14336, 4096, 8, False)):
+            codes, scl, wr, sr, kl = layer(K, N, b)
+            bias = bf16(rng.standard_normal(N) * 0.1) if with_bias else None
+            bias_d = torch.from_numpy(bias).to(dev).to(torch.bfloat16) if with_bias else None
+            th = [0.3, 0.6, 1.0, 1.5]
+            worst = (0.0, 0.0)
+            for it in range(4):
+                x = bf16(rng.standard_normal((M, K)))
+                xd = torch.from_numpy(x[:, rank * kl:(rank + 1) * kl]).to(dev).to(torch.bfloat16).contiguous()
+                y = linear_allreduce(xd, wr, sr, bias_d, b, 128, N // 4, th, peers)
+                if it == 1:
+                    gemv_allreduce(xd[:1], wr, sr, bias_d, b, 128, N // 4, th, peers)
+                ys = [torch.empty_like(y) for _ in range(world)]
+                dist.all_gather(ys, y)
+                same = all(torch.equal(ys[0], t) for t in ys)
+                ref = O.to_f32(O.gemm_or_gemv(x, codes, scl, bias, b, 128, th, "bf16"), "bf16")
+                mx, fr = _rel(y.float().cpu().numpy(), ref)
+                worst = (max(worst[0], mx), max(worst[1], fr))
+                ok = ok and same and mx <= MAX_REL_TOL and fr <= FRO_TOL
+                if not same:
+                    lines.append(f"M={M} K={K} N={N} it={it}: ranks differ")
+            lines.append(f"M={M} K={K} N={N} b={b} bias={with_bias}: worst max-rel {worst[0]:.2e} fro {worst[1]:.2e}")
+            if not agree(ok):
                 raise RuntimeError("; ".join(lines))
 
         # CUDA graph: three launches recorded, replayed with new inputs
@@ -190,6 +220,65 @@ def _worker(rank, world, port, q):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         lines.append(f"K={K} N={N} TP={world}: eager fused {t[0].item():.1f} us, eager gemv + NCCL all-reduce "
                      f"{t[1].item():.1f} us; graph fused {t[2].item():.1f} us, graph gemv alone {t[3].item():.1f} us")
+        # batch-64 decode at TP 2 (o and down of Llama-3-8B): the fused skinny GEMM
+        # against the same GEMM followed by an NCCL all-reduce, both replayed from
+        # CUDA graphs (the NCCL call captured in the graph) and eager
+        for name, (K, N) in (("o", (4096, 4096)), ("down", (14336, 4096))):
+            M, b = 64, 8
+            codes, scl, wr, sr, kl = layer(K, N, b)
+            xd = torch.from_numpy(bf16(rng.standard_normal((M, K)))[:, rank * kl:(rank + 1) * kl]).to(dev).to(
+                torch.bfloat16).contiguous()
+            th = [0.3, 0.6, 1.0, 1.5]
+
+            def fused_rows():
+                return linear_allreduce(xd, wr, sr, None, b, 128, N // 4, th, peers)
+
+            def gemm_nccl():
+                y = torch.ops.grinqh.gemm_or_gemv(xd, wr, sr, None, b, 128, N // 4, th, False)
+                dist.all_reduce(y)
+                return y
+
+            rt = {}
+            for tag, fn in (("fused", fused_rows), ("gemm+nccl", gemm_nccl)):
+                for _ in range(10):
+                    fn()
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(100):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                rt[tag] = e0.elapsed_time(e1) * 1e3 / 100
+                st = torch.cuda.Stream(dev)
+                st.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(st):
+                    fn()
+                torch.cuda.current_stream(dev).wait_stream(st)
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=st):
+                    for _ in range(20):
+                        fn()
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                gr.replay()
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                e0.record()
+                for _ in range(5):
+                    gr.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                rt[tag + " graph"] = e0.elapsed_time(e1) * 1e3 / 100
+                del gr
+            t = torch.tensor([rt["fused"], rt["gemm+nccl"], rt["fused graph"], rt["gemm+nccl graph"]], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            lines.append(f"{name} M=64 K={K} N={N} TP={world}: eager fused {t[0].item():.1f} us vs GEMM + NCCL "
+                         f"{t[1].item():.1f} us; graph fused {t[2].item():.1f} us vs GEMM + NCCL {t[3].item():.1f} us")
+
         from grinqh._ext import cabi
         import ctypes
         n_to = ctypes.c_uint(0)

@@ -442,9 +442,36 @@ static unsigned long long allreduce_wait_ns() {
   return (unsigned long long)ms * 1000000ull;
 }
 
-extern "C" size_t grinqh_allreduce_buffer_bytes(int world, int64_t max_n) {
-  if (world < 1 || world > kArMaxRanks || max_n <= 0) return 0;
-  return m1_allreduce_buffer_bytes(world, max_n);
+extern "C" size_t grinqh_allreduce_buffer_bytes(int world, int64_t cap) {
+  if (world < 1 || world > kArMaxRanks || cap <= 0) return 0;
+  return peer_reduce_buffer_bytes(world, cap);
+}
+
+// Which kernel a fused launch of M rows runs: one row graded (or union) by the
+// single-row kernel, 2..kSkinnyMaxRows dense rows by the skinny GEMM; 0 if neither.
+enum { kArNone = 0, kArM1 = 1, kArSkinny = 2 };
+static int allreduce_kernel(int km, int64_t M, int64_t K, int64_t N, int group) {
+  if (M == 1 && use_m1(km, M, K, N, group)) return kArM1;
+  if (use_skinny(km, M, K, N, group)) return kArSkinny;
+  return kArNone;
+}
+
+extern "C" size_t grinqh_allreduce_workspace_size(int64_t M, int64_t K, int64_t N, int max_bits, int group_size,
+                                                  int mode) {
+  if (group_size <= 0 || !valid_bits(max_bits) || M <= 0 || K <= 0 || N <= 0) return 0;
+  const int km = resolve_mode(mode & ~GRINQH_WORKSPACE_ZEROED, M);
+  if (km < 0) return 0;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices && g_sm_count[dev] > 0) sms = g_sm_count[dev];
+  switch (allreduce_kernel(km, M, K, N, group_size)) {
+    case kArM1: return workspace_for(plan_m1(K, N, group_size, sms));
+    case kArSkinny: {
+      SkinnyPlan plan{};
+      return plan_skinny_resident(M, K, N, sms, &plan) ? workspace_for(plan) : 0;
+    }
+    default: return 0;
+  }
 }
 
 extern "C" int grinqh_allreduce_buffer_alloc(size_t bytes, void** buf) {
@@ -494,47 +521,100 @@ extern "C" int grinqh_ipc_close_handle(void* buf) {
   return e == cudaSuccess ? GRINQH_OK : set_error(GRINQH_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
 }
 
-extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const uint32_t* w, const void* s,
-                                     const void* bias, int max_bits, int group, int64_t N, const float* thresholds,
-                                     void* y, void* workspace, size_t workspace_bytes, int rank, int world,
-                                     void* const* buffers, int64_t n_cap, int mode, grinqh_stream_t stream) {
+extern "C" int grinqh_gemm_allreduce(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                     const void* s, const void* bias, int max_bits, int group, int64_t N,
+                                     const float* thresholds, int mode, void* y, void* workspace,
+                                     size_t workspace_bytes, int rank, int world, void* const* buffers, int64_t cap,
+                                     grinqh_stream_t stream) {
   int dev = 0, sms = 0;
   GRINQH_RETURN_IF(device_info(&dev, &sms));
-  GRINQH_RETURN_IF(validate(x, dtype, 1, K, w, s, max_bits, group, N, y));
-  GRINQH_REQUIRE(thresholds, "thresholds required");
+  GRINQH_RETURN_IF(validate(x, dtype, M, K, w, s, max_bits, group, N, y));
+  const bool zeroed = (mode & GRINQH_WORKSPACE_ZEROED) != 0;
+  const int km = resolve_mode(mode & ~GRINQH_WORKSPACE_ZEROED, M);
+  GRINQH_REQUIRE(km >= 0, "unknown mode %d", mode & ~GRINQH_WORKSPACE_ZEROED);
+  GRINQH_REQUIRE(km == kModeDense || thresholds, "thresholds required for graded modes");
   GRINQH_REQUIRE(world >= 1 && world <= kArMaxRanks && rank >= 0 && rank < world, "rank %d of %d (at most %d ranks)",
                  rank, world, kArMaxRanks);
-  GRINQH_REQUIRE(buffers && N <= n_cap, "peer buffers hold %lld columns, N is %lld", (long long)n_cap, (long long)N);
+  GRINQH_REQUIRE(buffers && M * N <= cap, "peer buffers hold %lld values, M * N is %lld", (long long)cap,
+                 (long long)(M * N));
   for (int r = 0; r < world; ++r) GRINQH_REQUIRE(buffers[r] && aligned(buffers[r], 256), "peer buffer %d", r);
-  if (!m1_supported(1, K, N, group) || !m1_pointers_ok(w, s) || !m1_plan_fits(plan_m1(K, N, group, sms)))
-    return set_error(GRINQH_ERR_UNSUPPORTED, "fused all-reduce: shape or alignment not supported by the GEMV");
-  const bool zeroed = (mode & GRINQH_WORKSPACE_ZEROED) != 0;
-  const M1Plan plan = plan_m1(K, N, group, sms);
+  PeerReduce ar{};
+  ar.rank = rank;
+  ar.world = world;
+  ar.cap = cap;
+  ar.wait_ns = allreduce_wait_ns();
+  for (int r = 0; r < world; ++r) ar.buf[r] = static_cast<unsigned char*>(buffers[r]);
+  if (M == 0) return GRINQH_OK;  // every rank skips alike: no epoch is used
+  const int which = allreduce_kernel(km, M, K, N, group);
+
+  if (which == kArM1) {
+    if (!m1_pointers_ok(w, s) || !m1_plan_fits(plan_m1(K, N, group, sms)))
+      return set_error(GRINQH_ERR_UNSUPPORTED, "fused all-reduce not supported: shape or alignment of the "
+                       "single-row GEMV");
+    const M1Plan plan = plan_m1(K, N, group, sms);
+    const size_t need = workspace_for(plan);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+      return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
+    M1Args g{};
+    g.x = x;
+    g.w = w;
+    g.s = s;
+    g.bias = bias;
+    g.y = y;
+    g.K = (int)K;
+    g.N = (int)N;
+    g.group = group;
+    g.rows_per_warp = plan.rows_per_warp;
+    g.rows_per_cta = plan.rows_per_cta;
+    for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
+    g.ar = ar;
+    if (need > 0)
+      GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
+                                      &g.counters));
+    return launch_m1(g, plan, dtype, max_bits / 2, stream, true);
+  }
+
+  SkinnyPlan plan{};
+  if (which != kArSkinny || !skinny_pointers_ok(x, w, s) || !plan_skinny_resident(M, K, N, sms, &plan))
+    return set_error(GRINQH_ERR_UNSUPPORTED,
+                     "fused all-reduce not supported: M=%lld K=%lld N=%lld mode %d (the fused kernels take one "
+                     "graded row, or 2..%lld dense rows, with aligned views)",
+                     (long long)M, (long long)K, (long long)N, mode & ~GRINQH_WORKSPACE_ZEROED,
+                     (long long)kSkinnyMaxRows);
   const size_t need = workspace_for(plan);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return set_error(GRINQH_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
   GRINQH_REQUIRE(need == 0 || aligned(workspace, 256), "workspace must be 256-byte aligned");
-  M1Args g{};
+  SkinnyArgs g{};
   g.x = x;
   g.w = w;
   g.s = s;
   g.bias = bias;
   g.y = y;
+  g.M = (int)M;
   g.K = (int)K;
   g.N = (int)N;
   g.group = group;
-  g.rows_per_warp = plan.rows_per_warp;
-  g.rows_per_cta = plan.rows_per_cta;
-  for (int z = 0; z < 4; ++z) g.t[z] = thresholds[z];
-  g.ar.rank = rank;
-  g.ar.world = world;
-  g.ar.wait_ns = allreduce_wait_ns();
-  g.ar.n_cap = (int)n_cap;
-  for (int r = 0; r < world; ++r) g.ar.buf[r] = static_cast<unsigned char*>(buffers[r]);
+  g.tiles = plan.tiles;
+  g.splits = plan.splits;
+  g.cluster = plan.cluster;
+  g.steps_per_split = plan.steps_per_split;
+  g.ar = ar;
   if (need > 0)
     GRINQH_RETURN_IF(bind_workspace(workspace, plan.slot_bytes, plan.counter_bytes, zeroed, stream, &g.slots,
                                     &g.counters));
-  return launch_m1(g, plan, dtype, max_bits / 2, stream, true);
+  return launch_skinny(g, plan, dtype, max_bits / 2, stream, true);
+}
+
+extern "C" int grinqh_gemv_allreduce(const void* x, int dtype, int64_t K, const uint32_t* w, const void* s,
+                                     const void* bias, int max_bits, int group, int64_t N, const float* thresholds,
+                                     void* y, void* workspace, size_t workspace_bytes, int rank, int world,
+                                     void* const* buffers, int64_t n_cap, int mode, grinqh_stream_t stream) {
+  GRINQH_REQUIRE((mode & ~GRINQH_WORKSPACE_ZEROED) == 0, "mode takes only GRINQH_WORKSPACE_ZEROED");
+  GRINQH_REQUIRE(thresholds, "thresholds required");
+  return grinqh_gemm_allreduce(x, dtype, 1, K, w, s, bias, max_bits, group, N, thresholds, mode | GRINQH_MODE_AUTO,
+                               y, workspace, workspace_bytes, rank, world, buffers, n_cap, stream);
 }
 
 extern "C" int grinqh_take_error_flags(unsigned* timeouts) {

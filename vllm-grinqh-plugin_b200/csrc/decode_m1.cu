@@ -192,82 +192,26 @@ __device__ __forceinline__ void warp_chunk(const M1Args& a, int tile, int kb, in
 }
 
 // ---------------------------------------------------------------- fused all-reduce
-// Partials travel as 64-bit words {fp32 bits, epoch}: a naturally aligned 64-bit
-// store is single-copy atomic, so a reader that sees this launch's epoch in a word
-// also sees the value stored with it, without a fence or a separate flag.
-__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Runs in the CTA that finalises column slice `tile`, after it has stored the slice's
 // sums into every rank's buffer: waits (bounded) until every rank's partial of each of
-// this thread's columns carries this launch's epoch, then adds them in rank order --
-// the same order on every rank, so all ranks get the same bits -- adds the bias and
-// writes y. The slices finalise independently; a waiting CTA waits only on the peer
-// CTAs that finalise the same slice, which wait on nothing on their own GPU.
+// this thread's columns carries this launch's epoch, adds them in rank order, adds the
+// bias and writes y. The slices finalise independently; a waiting CTA waits only on the
+// peer CTAs that finalise the same slice, which wait on nothing on their own GPU.
 template <typename T>
 __device__ void allreduce_tail(const M1Args& a, int tile, unsigned epoch) {
   constexpr int kH = kSliceN / kThreads;
-  const M1AllReduce& ar = a.ar;
   const int n16 = a.N >> 4;
-  const unsigned long long* parts = reinterpret_cast<const unsigned long long*>(ar.buf[ar.rank] + kArParts) +
-                                    (size_t)(epoch & 1u) * ar.world * ar.n_cap;
-  int nn[kH];
+  size_t nn[kH];
   bool ok[kH];
 #pragma unroll
-  for (int h = 0; h < kH; ++h) {  // the columns store_y wrote for this thread
+  for (int h = 0; h < kH; ++h) {  // the columns store_y published for this thread
     const int col = threadIdx.x + h * kThreads;
     const int jx = tile * kSliceW + col % kSliceW;
     ok[h] = jx < n16;
-    nn[h] = (col / kSliceW) * n16 + jx;
+    nn[h] = (size_t)(col / kSliceW) * n16 + jx;
   }
-  // two ranks at a time (2 * kH words in flight), each added in rank order
   float v[kH];
-#pragma unroll
-  for (int h = 0; h < kH; ++h) v[h] = 0.f;
-  uint64_t t0 = 0;
-  bool gave_up = false;
-  for (int r0 = 0; r0 < ar.world && !gave_up; r0 += 2) {
-    const int nr = min(2, ar.world - r0);
-    unsigned long long q[2][kH];
-    for (uint32_t it = 0;; ++it) {
-      bool all = true;
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int h = 0; h < kH; ++h)
-          if (j < nr && ok[h] && (it == 0 || (unsigned)(q[j][h] >> 32) != epoch))
-            q[j][h] = ld_relaxed_sys_u64(parts + (size_t)(r0 + j) * ar.n_cap + nn[h]);
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int h = 0; h < kH; ++h)
-          if (j < nr && ok[h] && (unsigned)(q[j][h] >> 32) != epoch) all = false;
-      if (all) break;
-      if (t0 == 0) t0 = globaltimer_ns();
-      if ((it & 63u) == 63u) {
-        // after any wait of this library gave up, give up at once (the output is
-        // invalid anyway and the host sees the count); else after kWaitNs
-        if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) != 0u ||
-            globaltimer_ns() - t0 > ar.wait_ns) {  // a rank never arrived
-          if (*reinterpret_cast<volatile unsigned*>(&g_wait_timeouts) == 0u) atomicAdd(&g_wait_timeouts, 1u);
-          gave_up = true;
-          break;
-        }
-      }
-      __nanosleep(32);
-    }
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int h = 0; h < kH; ++h)
-        if (j < nr) v[h] += __uint_as_float((unsigned)q[j][h]);
-  }
+  peer_sum<kH>(a.ar, epoch, nn, ok, v);  // on a timeout y is invalid; the host sees the count
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
 #pragma unroll
@@ -276,25 +220,6 @@ __device__ void allreduce_tail(const M1Args& a, int tile, unsigned epoch) {
     T out = Act<T>::from_f(v[h]);
     if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[nn[h]]));
     y[nn[h]] = out;
-  }
-}
-
-// Every CTA of a fused launch calls this as it exits. The epoch of a launch is read by
-// each CTA when it starts, so the next epoch may only be published once every CTA of
-// the grid has started: the last CTA to finish (a grid-wide count in the buffer's
-// word 1) publishes it and clears the count. The next launch reads it after
-// griddepcontrol.wait, i.e. after this grid has completed.
-template <bool kAR>
-__device__ __forceinline__ void ar_cta_done(const M1Args& a, unsigned epoch) {
-  if constexpr (kAR) {
-    if (threadIdx.x == 0) {
-      unsigned* words = reinterpret_cast<unsigned*>(a.ar.buf[a.ar.rank]);
-      __threadfence();  // this CTA's read of the epoch is ordered before its count
-      if (atomicAdd(words + 1, 1u) == gridDim.x * gridDim.y - 1u) {
-        words[1] = 0u;
-        *reinterpret_cast<volatile unsigned*>(words) = epoch;
-      }
-    }
   }
 }
 
@@ -333,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   }
   wait_prior_grid();  // x and the outputs belong to the stream order from here on
   // epoch of this launch (fused all-reduce): one more than the last completed one
-  const unsigned ar_epoch = kAR ? *reinterpret_cast<volatile unsigned*>(a.ar.buf[a.ar.rank]) + 1u : 0u;
+  const unsigned ar_epoch = kAR ? peer_epoch(a.ar) : 0u;
   warp_chunk<NZ, T>(a, tile, rb, re, rows + (rb - k0), wacc);
   allow_dependent_grid();
 
@@ -362,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   }
   cluster.sync();  // other ranks keep their shared memory alive until rank 0 has read it
   if (crank != 0) {
-    ar_cta_done<kAR>(a, ar_epoch);
+    peer_cta_done<kAR>(a.ar, ar_epoch);
     return;
   }
 
@@ -374,10 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
     if (jx >= n16) return;
     const int nn = c * n16 + jx;
     if constexpr (kAR) {  // this rank's partial, into every rank's buffer (NVLink stores)
-      const size_t off = ((size_t)(ar_epoch & 1u) * a.ar.world + a.ar.rank) * a.ar.n_cap + nn;
-      const unsigned long long word = ((unsigned long long)ar_epoch << 32) | __float_as_uint(v);
-      for (int r = 0; r < a.ar.world; ++r)
-        st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.ar.buf[r] + kArParts) + off, word);
+      peer_publish(a.ar, ar_epoch, (size_t)nn, v);
       return;
     }
     T out = Act<T>::from_f(v);
@@ -389,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
 #pragma unroll
     for (int h = 0; h < kSliceN / kThreads; ++h) store_y(threadIdx.x + h * kThreads, sum2[h]);
     if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
-    ar_cta_done<kAR>(a, ar_epoch);
+    peer_cta_done<kAR>(a.ar, ar_epoch);
     return;
   }
   const int clu = split / csize;
@@ -401,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   if (threadIdx.x == 0) s_last = atomicAdd(a.counters + tile, 1u) == (unsigned)(nclu - 1);
   __syncthreads();
   if (!s_last) {
-    ar_cta_done<kAR>(a, ar_epoch);
+    peer_cta_done<kAR>(a.ar, ar_epoch);
     return;
   }
   __threadfence();
@@ -421,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 2) m1_kernel(const M1Args a) {
   }
   if (threadIdx.x == 0) a.counters[tile] = 0u;  // ready for the next launch
   if constexpr (kAR) allreduce_tail<T>(a, tile, ar_epoch);
-  ar_cta_done<kAR>(a, ar_epoch);
+  peer_cta_done<kAR>(a.ar, ar_epoch);
 }
 
 template <int NZ, typename T, bool kAR>

@@ -5,21 +5,9 @@
 #include <stddef.h>
 #include <stdint.h>
 
-namespace grinqh {
+#include "peer_reduce.cuh"
 
-// Fused all-reduce over the tensor-parallel ranks' peer buffers (grinqh_gemv_allreduce).
-// Buffer of a rank: word 0 = epoch of its last completed launch, word 1 = count of this
-// launch's CTAs that have finished (the last one publishes the epoch and clears the
-// count); at kArParts the partial sums [2 (epoch parity)][world][n_cap], each a 64-bit
-// word {fp32 bits, epoch} written by the rank that computed it (the epoch in the word
-// tells the reader it is current).
-constexpr int kArMaxRanks = 8;
-constexpr size_t kArParts = 256;
-struct M1AllReduce {
-  unsigned char* buf[kArMaxRanks];  // every rank's buffer as mapped in this process
-  int rank, world, n_cap;
-  unsigned long long wait_ns;       // a peer's partial not seen after this long: give up
-};
+namespace grinqh {
 
 struct M1Args {
   const void* x;        // [K] dtype
@@ -31,7 +19,7 @@ struct M1Args {
   unsigned* counters;   // [tiles] tickets; zero before the first launch, left zero
   int K, N, group, rows_per_warp, rows_per_cta;
   float t[4];
-  M1AllReduce ar;       // used by the fused all-reduce launch only
+  PeerReduce ar;        // used by the fused all-reduce launch only (cap >= N)
 };
 
 struct M1Plan {
@@ -57,8 +45,5 @@ int launch_m1(const M1Args& a, const M1Plan& p, int dtype, int nz, cudaStream_t 
 // Reads and clears the count of fused all-reduce waits that gave up (this file's copy
 // of the bounded-wait counter).
 unsigned take_m1_timeouts();
-inline size_t m1_allreduce_buffer_bytes(int world, int64_t n_cap) {
-  return kArParts + 2 * (size_t)world * (size_t)n_cap * sizeof(uint64_t);
-}
 
 }  // namespace grinqh

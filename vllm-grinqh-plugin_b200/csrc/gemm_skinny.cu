@@ -32,8 +32,18 @@
 // result; otherwise it goes to an fp32 slot and the last cluster to finish a share
 // (atomic ticket) adds the clusters' slots in order. Deterministic; every wait is
 // bounded.
+//
+// Fused all-reduce (kAR, tensor-parallel row-parallel layers): where a CTA would write
+// an entry of y it stores its fp32 value, tagged with the launch epoch, into every
+// rank's peer buffer instead (peer_reduce.cuh), then waits for every rank's value of
+// the same entries, adds them in rank order and writes y. A CTA waits on peer CTAs
+// only, never on another CTA of its own grid, but the peer CTAs must be running: the
+// host keeps the whole grid resident at once (plan_skinny_resident).
 #include <cooperative_groups.h>
 #include <cuda.h>
+
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm_skinny.cuh"
@@ -94,7 +104,7 @@ __device__ __forceinline__ uint64_t* bar_at(unsigned char* smem, int i) {
   return reinterpret_cast<uint64_t*>(smem + kOffBar) + i;
 }
 
-template <int NZ, typename T>
+template <int NZ, typename T, bool kAR>
 __global__ void __launch_bounds__(kThreads, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                   const SkinnyArgs a, const int mp) {
@@ -113,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = bar_at(smem, 2 * SP + 3 * SW);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_at(smem, 2 * SP + 3 * SW + 1));
   __shared__ int s_last;
+  __shared__ unsigned s_epoch;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -344,6 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  // fused all-reduce: the epoch of this launch (thread 0 is past wait_prior_grid)
+  if constexpr (kAR)
+    if (threadIdx.x == 0) s_epoch = peer_epoch(a.ar);
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) tmem_dealloc(tmem, tcols);
@@ -352,6 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   T* y = static_cast<T*>(a.y);
   const T* bias = static_cast<const T*>(a.bias);
   const float* part = reinterpret_cast<const float*>(smem);
+  const unsigned epoch = kAR ? s_epoch : 0u;
   // (row m, column group c, word w) -> y[m, c * n16 + jt0 + w]; one warp writes a
   // pair's 32 words (64 contiguous bytes)
   auto store_y = [&](int m, int c, int w, float v) {
@@ -361,10 +376,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (bias) out = Act<T>::from_f(Act<T>::to_f(out) + Act<T>::to_f(bias[n]));
     y[(size_t)m * a.N + n] = out;
   };
+  // the final K sum of an entry: y, or with the fused all-reduce this rank's partial,
+  // stored into every rank's buffer (a warp stores a pair's 32 words, 256 contiguous
+  // bytes, into each); the ranks' sums follow in peer_gather
+  auto finish = [&](int m, int c, int w, float v) {
+    if constexpr (kAR) {
+      if (m >= a.M || jt0 + w >= n16) return;
+      peer_publish(a.ar, epoch, (size_t)m * a.N + c * n16 + jt0 + w, v);
+    } else {
+      store_y(m, c, w, v);
+    }
+  };
+  // fused all-reduce, second half: for the pairs first, first + stride, ... (below
+  // npairs) that this warp published, every rank's partial summed in rank order (four
+  // pairs' words in flight at a time), the bias added, y written. A CTA waits only on
+  // the peer CTAs that publish the same entries, which publish before they wait.
   const int npairs = mp * 16;
+  auto peer_gather = [&](int first, int stride) {
+    if constexpr (kAR) {
+      for (int p0 = first; p0 < npairs; p0 += 4 * stride) {
+        size_t e[4];
+        bool ok[4];
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int pr = p0 + i * stride, m = pr >> 4;
+          ok[i] = pr < npairs && m < a.M && jt0 + lane < n16;
+          e[i] = (size_t)m * a.N + (pr & 15) * n16 + jt0 + lane;
+        }
+        peer_sum<4>(a.ar, epoch, e, ok, v);  // on a timeout y is invalid; the host sees the count
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (ok[i]) store_y((p0 + i * stride) >> 4, (p0 + i * stride) & 15, lane, v[i]);
+      }
+    }
+  };
   if (a.splits == 1) {
     for (int pr = warp; pr < npairs; pr += kThreads / 32)
-      store_y(pr >> 4, pr & 15, lane, part[(pr >> 4) * kPartRow + (pr & 15) * 33 + lane]);
+      finish(pr >> 4, pr & 15, lane, part[(pr >> 4) * kPartRow + (pr & 15) * 33 + lane]);
+    peer_gather(warp, kThreads / 32);
+    peer_cta_done<kAR>(a.ar, epoch);
     return;
   }
   cg::cluster_group cluster = cg::this_cluster();
@@ -380,26 +431,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int off = (pr >> 4) * kPartRow + (pr & 15) * 33 + lane;
     float v = 0.f;
     for (int r = 0; r < cs; ++r) v += cluster.map_shared_rank(part, r)[off];
-    if (nclu == 1) store_y(pr >> 4, pr & 15, lane, v);
+    if (nclu == 1) finish(pr >> 4, pr & 15, lane, v);
     else __stcg(myslot + (size_t)pr * 32 + lane, v);
   }
   cluster.sync();  // every rank keeps its shared memory until the others have read it
-  if (nclu == 1) return;
+  if (nclu == 1) {
+    peer_gather(crank + cs * warp, cs * (kThreads / 32));
+    peer_cta_done<kAR>(a.ar, epoch);
+    return;
+  }
   __threadfence();
   __syncthreads();
   unsigned* ticket = a.counters + (size_t)tile * cs + crank;
   if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1u) == (unsigned)(nclu - 1);
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    peer_cta_done<kAR>(a.ar, epoch);
+    return;
+  }
   __threadfence();
   for (int k = warp; crank + cs * k < npairs; k += kThreads / 32) {
     const int pr = crank + cs * k;
     float v = 0.f;
     for (int cl = 0; cl < nclu; ++cl)
       v += __ldcg(a.slots + ((size_t)tile * nclu + cl) * slot_elems + (size_t)pr * 32 + lane);
-    store_y(pr >> 4, pr & 15, lane, v);
+    finish(pr >> 4, pr & 15, lane, v);
   }
   if (threadIdx.x == 0) *ticket = 0u;  // ready for the next launch
+  peer_gather(crank + cs * warp, cs * (kThreads / 32));
+  peer_cta_done<kAR>(a.ar, epoch);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -418,7 +478,7 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int NZ, typename T>
+template <int NZ, typename T, bool kAR>
 int launch_t(const SkinnyArgs& a, const SkinnyPlan& p, cudaStream_t st) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -447,7 +507,7 @@ int launch_t(const SkinnyArgs& a, const SkinnyPlan& p, cudaStream_t st) {
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(GRINQH_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed (%d)", (int)r);
   }
-  auto kern = skinny_kernel<NZ, T>;
+  auto kern = skinny_kernel<NZ, T, kAR>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return set_error(GRINQH_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg{};
@@ -490,23 +550,20 @@ bool skinny_pointers_ok(const void* x, const void* w, const void* s) {
          (reinterpret_cast<uintptr_t>(s) % 4) == 0;
 }
 
-SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
+static SkinnyPlan plan_for(int64_t M, int64_t K, int64_t N, int64_t target, int max_cluster = 8) {
   SkinnyPlan p{};
   p.mp = (int)((M + 15) / 16 * 16);
   const int64_t n16 = N / 16;
   p.tiles = (int)((n16 + TW - 1) / TW);
   const int64_t nk = K / BK;
-  // one CTA per SM (about 200 KB of shared memory each); clusters of up to 8 pack
-  // into the GPCs less densely than single CTAs, so aim a little under the SM count
-  const int64_t target = (sm_count > 0 ? sm_count : 148) * 7 / 8;
   int64_t splits = target / p.tiles;
   if (splits > nk) splits = nk;
   if (splits < 1) splits = 1;
   int64_t steps = (nk + splits - 1) / splits;
   splits = (nk + steps - 1) / steps;  // no empty splits
-  // cluster: the largest size <= 8 that divides the split count
+  // cluster: the largest size <= max_cluster (8) that divides the split count
   int cl = 1;
-  for (int c = 8; c >= 1; --c)
+  for (int c = max_cluster; c >= 1; --c)
     if (splits % c == 0) {
       cl = c;
       break;
@@ -520,21 +577,87 @@ SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
   return p;
 }
 
-int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st) {
+SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
+  // one CTA per SM (about 200 KB of shared memory each); clusters of up to 8 pack
+  // into the GPCs less densely than single CTAs, so aim a little under the SM count
+  return plan_for(M, K, N, (int64_t)(sm_count > 0 ? sm_count : 148) * 7 / 8);
+}
+
+// Clusters of `cluster` CTAs that the current device holds at once. Every
+// instantiation of the kernel has the same block size, shared memory and register
+// bound (one CTA per SM), so one of them answers for all.
+static int resident_clusters(int cluster) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(dev, cluster);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kern = skinny_kernel<4, __nv_bfloat16, true>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, (unsigned)cluster, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)cluster;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+bool plan_skinny_resident(int64_t M, int64_t K, int64_t N, int sm_count, SkinnyPlan* out) {
+  int64_t target = (int64_t)(sm_count > 0 ? sm_count : 148) * 7 / 8;
+  for (;;) {
+    // the split count of plan_skinny with the largest cluster whose grid is resident
+    // (clusters live inside one GPC, so smaller ones pack the SMs more densely)
+    SkinnyPlan p{};
+    for (int cmax = 8; cmax >= 1; cmax = p.cluster - 1) {
+      p = plan_for(M, K, N, target, cmax);
+      const int have = resident_clusters(p.cluster);
+      if (have > 0 && (int64_t)p.tiles * p.splits <= (int64_t)have * p.cluster) {
+        *out = p;
+        return true;
+      }
+      if (have <= 0) return false;
+    }
+    if (p.splits == 1) return false;           // even one CTA per tile does not fit
+    target = (int64_t)p.tiles * p.splits - 1;  // fewer splits
+  }
+}
+
+template <bool kAR>
+static int launch_ar(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st) {
   if (dtype == GRINQH_BF16) {
     switch (nz) {
-      case 1: return launch_t<1, __nv_bfloat16>(a, p, st);
-      case 2: return launch_t<2, __nv_bfloat16>(a, p, st);
-      case 3: return launch_t<3, __nv_bfloat16>(a, p, st);
-      default: return launch_t<4, __nv_bfloat16>(a, p, st);
+      case 1: return launch_t<1, __nv_bfloat16, kAR>(a, p, st);
+      case 2: return launch_t<2, __nv_bfloat16, kAR>(a, p, st);
+      case 3: return launch_t<3, __nv_bfloat16, kAR>(a, p, st);
+      default: return launch_t<4, __nv_bfloat16, kAR>(a, p, st);
     }
   }
   switch (nz) {
-    case 1: return launch_t<1, __half>(a, p, st);
-    case 2: return launch_t<2, __half>(a, p, st);
-    case 3: return launch_t<3, __half>(a, p, st);
-    default: return launch_t<4, __half>(a, p, st);
+    case 1: return launch_t<1, __half, kAR>(a, p, st);
+    case 2: return launch_t<2, __half, kAR>(a, p, st);
+    case 3: return launch_t<3, __half, kAR>(a, p, st);
+    default: return launch_t<4, __half, kAR>(a, p, st);
   }
+}
+
+int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st, bool allreduce) {
+  return allreduce ? launch_ar<true>(a, p, dtype, nz, st) : launch_ar<false>(a, p, dtype, nz, st);
 }
 
 }  // namespace grinqh

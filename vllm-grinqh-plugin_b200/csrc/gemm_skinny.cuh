@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "peer_reduce.cuh"
+
 namespace grinqh {
 
 struct SkinnyArgs {
@@ -18,6 +20,7 @@ struct SkinnyArgs {
   unsigned* counters;   // [tiles, cluster size] tickets; zero before the first launch, left zero
   int M, K, N, group;
   int tiles, splits, cluster, steps_per_split;
+  PeerReduce ar;        // used by the fused all-reduce launch only (cap >= M * N)
 };
 
 struct SkinnyPlan {
@@ -29,7 +32,12 @@ struct SkinnyPlan {
 bool skinny_supported(int64_t M, int64_t K, int64_t N, int group);
 bool skinny_pointers_ok(const void* x, const void* w, const void* s);
 SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count);
-int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st);
+// The plan of the fused all-reduce launch: as plan_skinny, with fewer K splits where
+// needed so that the whole grid is resident at once (its CTAs wait on the peer ranks'
+// CTAs, which must all be running). False if no plan is.
+bool plan_skinny_resident(int64_t M, int64_t K, int64_t N, int sm_count, SkinnyPlan* out);
+int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st,
+                  bool allreduce = false);
 unsigned take_skinny_timeouts();
 
 }  // namespace grinqh

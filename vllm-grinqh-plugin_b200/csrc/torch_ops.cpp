@@ -198,6 +198,61 @@ at::Tensor gemv_allreduce(const at::Tensor& x, const at::Tensor& weight_packed, 
   return y.view(out_shape);
 }
 
+// Row-parallel linear of M rows with the tensor-parallel sum fused in (the C ABI's
+// grinqh_gemm_allreduce): one graded row or 2..64 dense rows; any other shape raises
+// "fused all-reduce not supported" before anything is launched (on every rank alike).
+at::Tensor linear_allreduce(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                            const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
+                            int64_t original_n, at::ArrayRef<double> thresholds, int64_t mode, int64_t rank,
+                            int64_t world, at::ArrayRef<int64_t> buffers, int64_t cap) {
+  const NvtxRange range("grinqh::linear_allreduce");
+  check_cuda(x, "x");
+  check_cuda(weight_packed, "weight_packed");
+  check_cuda(weight_scale, "weight_scale");
+  const int dt = dtype_code(x, "x");
+  TORCH_CHECK(weight_scale.scalar_type() == x.scalar_type(), "GRINQH: weight_scale dtype != x dtype");
+  TORCH_CHECK(is_word32(weight_packed) && weight_packed.dim() == 2 && weight_scale.dim() == 2,
+              "GRINQH: weight_packed must be 2-D int32/uint32 and weight_scale 2-D");
+  const int64_t K = weight_packed.size(0), N = original_n * 4;
+  TORCH_CHECK(x.dim() >= 1 && x.size(-1) == K, "GRINQH linear_allreduce: x must be [..., K] with K = ", K);
+  TORCH_CHECK(max_bits == 2 || max_bits == 4 || max_bits == 6 || max_bits == 8,
+              "GRINQH: max_bits must be 2, 4, 6 or 8, got ", max_bits);
+  TORCH_CHECK(weight_packed.size(1) == (max_bits / 2) * (N / 16), "GRINQH: weight_packed has ", weight_packed.size(1),
+              " columns, expected ", (max_bits / 2) * (N / 16), " for N=", N, " and max_bits=", max_bits);
+  TORCH_CHECK(group_size > 0 && K % group_size == 0 && weight_scale.size(0) == K / group_size &&
+                  weight_scale.size(1) == N,
+              "GRINQH: weight_scale shape ", weight_scale.sizes(), " does not match K=", K, ", N=", N);
+  TORCH_CHECK((int64_t)buffers.size() == world, "GRINQH linear_allreduce: one buffer per rank");
+  if (bias) {
+    check_cuda(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == x.scalar_type() && bias->numel() == N, "GRINQH: bias must be [N] of x's dtype");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor xf = x.reshape({-1, K}).contiguous();
+  const int64_t M = xf.size(0);
+  const at::Tensor wp = weight_packed.contiguous();
+  const at::Tensor sc = weight_scale.contiguous();
+  const at::Tensor bc = bias ? bias->contiguous() : at::Tensor();
+  std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
+  out_shape.back() = N;
+  at::Tensor y = at::empty({M, N}, x.options());
+  const auto th = thresholds4(thresholds);
+  const size_t ws_bytes = grinqh_allreduce_workspace_size(M, K, N, (int)max_bits, (int)group_size, (int)mode);
+  const cudaStream_t stream = cur_stream(x);
+  at::Tensor ws;
+  bool zeroed = false;
+  if (ws_bytes) ws = stream_workspace(x, ws_bytes, stream, &zeroed);
+  std::vector<void*> bufs(buffers.size());
+  for (size_t r = 0; r < buffers.size(); ++r) bufs[r] = reinterpret_cast<void*>(buffers[r]);
+  check_ok(grinqh_gemm_allreduce(xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()),
+                                 sc.data_ptr(), bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N,
+                                 th.data(), zeroed ? ((int)mode | GRINQH_WORKSPACE_ZEROED) : (int)mode, y.data_ptr(),
+                                 ws_bytes ? ws.data_ptr() : nullptr, ws_bytes ? static_cast<size_t>(ws.numel()) : 0,
+                                 (int)rank, (int)world, bufs.data(), cap, stream),
+           "linear_allreduce");
+  return y.view(out_shape);
+}
+
 // torch.ops.grinqh.gemm_or_gemv -- grinqh/kernel.py:646-710. use_marlin is accepted
 // for schema compatibility and ignored (no Marlin path in this build).
 at::Tensor gemm_or_gemv(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
@@ -313,6 +368,9 @@ TORCH_LIBRARY(grinqh, m) {
   m.def("unpack_checkpoint(Tensor src, int max_bits, int row0, int rows, int k0, Tensor(a!) dst, int n_off) -> ()");
   m.def("gemv_allreduce(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
         "int group_size, int original_n, float[] thresholds, int rank, int world, int[] buffers, int n_cap) -> Tensor");
+  m.def("linear_allreduce(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
+        "int group_size, int original_n, float[] thresholds, int mode, int rank, int world, int[] buffers, "
+        "int cap) -> Tensor");
   m.def("grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor)");
 }
 
@@ -324,5 +382,6 @@ TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
   m.impl("unpack", &unpack);
   m.impl("unpack_checkpoint", &unpack_checkpoint);
   m.impl("gemv_allreduce", &gemv_allreduce);
+  m.impl("linear_allreduce", &linear_allreduce);
   m.impl("grade", &grade);
 }

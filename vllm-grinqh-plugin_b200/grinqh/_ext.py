@@ -39,6 +39,9 @@ SIGNATURES = {
     "grinqh_ipc_close_handle": (_int, [_ptr]),
     "grinqh_gemv_allreduce": (_int, [_ptr, _int, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _ptr, _ptr, _ptr,
                                      ctypes.c_size_t, _int, _int, _ptr, _i64, _int, _ptr]),
+    "grinqh_allreduce_workspace_size": (_size, [_i64, _i64, _i64, _int, _int, _int]),
+    "grinqh_gemm_allreduce": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr, _int,
+                                     _ptr, _ptr, _size, _int, _int, _ptr, _i64, _ptr]),
     "grinqh_unpack": (_int, [_ptr, _ptr, _i64, _i64, _int, _ptr]),
     "grinqh_grade": (_int, [_ptr, _int, _i64, _i64, _fptr, _int, _ptr, _ptr, _ptr]),
     "grinqh_workspace_size": (_size, [_i64, _i64, _i64, _int, _int, _int]),

@@ -234,7 +234,8 @@ class GRINQHLinearMethod(LinearMethodBase):
         layer.grinqh_use_marlin = False
         # GRINQH_FUSED_ALLREDUCE=1: a row-parallel layer whose output vLLM would
         # all-reduce does the reduction itself (grinqh.allreduce.row_parallel_linear:
-        # single rows in one GEMV + NVLink-sum kernel). Layers built with
+        # one row in one GEMV + NVLink-sum kernel, 2..64 rows in one skinny GEMM +
+        # NVLink-sum kernel). Layers built with
         # reduce_results=False (the model reduces elsewhere) are left alone.
         layer.grinqh_fused_allreduce = False
         if (os.environ.get("GRINQH_FUSED_ALLREDUCE") == "1" and hasattr(layer, "input_is_parallel")
@@ -243,8 +244,8 @@ class GRINQHLinearMethod(LinearMethodBase):
             layer.grinqh_fused_allreduce = True
             # the peer buffers are set up here, at load time (collective over the TP
             # group, same layer order on every rank), never inside graph capture
-            from .allreduce import tp_peers
-            tp_peers(packed.device, 4 * layer.original_n)
+            from .allreduce import FUSED_MAX_ROWS, tp_peers
+            tp_peers(packed.device, FUSED_MAX_ROWS * 4 * layer.original_n)
 
     def apply(self, layer: torch.nn.Module, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
         if getattr(layer, "grinqh_fused_allreduce", False):

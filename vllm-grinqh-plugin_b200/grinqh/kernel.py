@@ -55,6 +55,12 @@ def _fake_gemv_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_s
     return x.new_empty((*x.shape[:-1], 4 * original_n))
 
 
+@torch.library.register_fake("grinqh::linear_allreduce")
+def _fake_linear_allreduce(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds, mode,
+                           rank, world, buffers, cap):
+    return x.new_empty((*x.shape[:-1], 4 * original_n))
+
+
 @torch.library.register_fake("grinqh::unpack_checkpoint")
 def _fake_unpack_checkpoint(src, max_bits, row0, rows, k0, dst, n_off):
     return None
