@@ -45,6 +45,7 @@ import torch.distributed as dist  # noqa: E402
 SHAPES = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 28672), "down": (14336, 4096)}
 GROUP = 128
 QUANTILES = [0.2, 0.4, 0.6, 0.8]
+FUSED_MAX_ROWS = 64  # rows the fused row-parallel kernels take (grinqh.allreduce.FUSED_MAX_ROWS)
 
 
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "m1_kernel_gate_up_b8_graded.md")
@@ -255,7 +256,8 @@ def run_ours(args, rank, world, dev):
     two weight copies rotated. Several GPUs (default): tensor parallelism as vLLM
     shards the layer -- qkv and gate_up column parallel, o and down row parallel with
     the ranks' partial sums added in the step (the fused GEMV + all-reduce kernel for
-    one row, the GEMM followed by NCCL's all-reduce for more rows)."""
+    one row, the fused skinny GEMM + all-reduce kernel for 2..64 rows, the GEMM followed
+    by NCCL's all-reduce for more rows)."""
     from grinqh.kernel import grinqh_gemm_or_gemv
     bits, M = args.bits, args.m
     torch.cuda.set_device(dev)
@@ -293,9 +295,9 @@ def run_ours(args, rank, world, dev):
     ctrl = None
     if tp:
         ctrl = dist.new_group(backend="gloo")
-        if graded:
+        if M <= FUSED_MAX_ROWS:
             from grinqh.allreduce import PeerBuffers
-            peers = PeerBuffers(ctrl, n_cap=max(SHAPES[n][1] for n in ROW_PARALLEL), device=dev)
+            peers = PeerBuffers(ctrl, n_cap=M * max(SHAPES[n][1] for n in ROW_PARALLEL), device=dev)
 
     def run_linear(c, name, fused=True):
         w, s = layers[c][name]
@@ -304,6 +306,9 @@ def run_ours(args, rank, world, dev):
             if graded:
                 from grinqh.allreduce import gemv_allreduce
                 return gemv_allreduce(x_in[name], w, s, None, bits, GROUP, nl // 4, ths[name], peers)
+            if M <= FUSED_MAX_ROWS:
+                from grinqh.allreduce import linear_allreduce
+                return linear_allreduce(x_in[name], w, s, None, bits, GROUP, nl // 4, ths[name], peers)
             y = grinqh_gemm_or_gemv(x_in[name], w, s, None, bits, GROUP, nl // 4, ths[name])
             dist.all_reduce(y)
             return y
@@ -396,7 +401,9 @@ def run_ours(args, rank, world, dev):
 
     if tp:
         parallelism = (f"tp{world}: qkv / gate_up column parallel, o / down row parallel with the sum "
-                       + ("fused into the GEMV (NVLink peer stores)" if graded else "by NCCL all-reduce"))
+                       + ("fused into the GEMV (NVLink peer stores)" if graded else
+                          "fused into the skinny GEMM (NVLink peer stores)" if M <= FUSED_MAX_ROWS
+                          else "by NCCL all-reduce"))
     else:
         parallelism = f"replicas x{world} (no collective on the data path)"
     line = {
@@ -487,7 +494,8 @@ def run_e2e(args, dev, stream, layers, ncopies, x_in, xs, ths, local, peers, tp,
     """The step end to end through the C ABI (include/grinqh_b200.h) with host buffers:
     per step one pinned H2D of the step's activations (every linear's input, back to
     back), the four linears (grinqh_gemm_or_gemv; the row-parallel ones of a sharded
-    layer through grinqh_gemv_allreduce for one row, or followed by NCCL's all-reduce),
+    layer through grinqh_gemv_allreduce for one row, grinqh_gemm_allreduce for 2..64
+    rows, or followed by NCCL's all-reduce),
     all writing one output buffer, and one D2H of it. Returns (ms per step, max over
     ranks; H2D bytes; D2H bytes)."""
     from grinqh._ext import cabi, check, thresholds_arg, GRINQH_BF16, MODE_AUTO
@@ -508,7 +516,8 @@ def run_e2e(args, dev, stream, layers, ncopies, x_in, xs, ths, local, peers, tp,
     host_y = torch.empty(ny, dtype=torch.bfloat16).pin_memory()
     dev_x = torch.empty(nx, dtype=torch.bfloat16, device=dev)
     dev_y = torch.empty(ny, dtype=torch.bfloat16, device=dev)
-    ws_bytes = max(lib.grinqh_workspace_size(M, K, N, bits, GROUP, MODE_AUTO) for K, N in local.values())
+    ws_bytes = max(max(lib.grinqh_workspace_size(M, K, N, bits, GROUP, MODE_AUTO),
+                       lib.grinqh_allreduce_workspace_size(M, K, N, bits, GROUP, MODE_AUTO)) for K, N in local.values())
     ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)  # tickets stay zero between calls
     th_args = {n: thresholds_arg(ths[n]) for n in names}
     workspace_zeroed = 0x100  # GRINQH_WORKSPACE_ZEROED
@@ -524,10 +533,16 @@ def run_e2e(args, dev, stream, layers, ncopies, x_in, xs, ths, local, peers, tp,
             K, N = local[n]
             w, s = layers[c][n]
             xp, yp = dev_x.data_ptr() + 2 * x_off[n], dev_y.data_ptr() + 2 * y_off[n]
-            if tp and n in ROW_PARALLEL and peers is not None:
+            if tp and n in ROW_PARALLEL and peers is not None and M == 1:
                 check(lib.grinqh_gemv_allreduce(xp, GRINQH_BF16, K, w.data_ptr(), s.data_ptr(), None, bits, GROUP, N,
                                                 th_args[n], yp, ws.data_ptr(), ws.numel(), peers.rank, peers.world,
-                                                bufs, peers.n_cap, MODE_AUTO | workspace_zeroed, st), f"e2e {n}")
+                                                bufs, peers.n_cap, workspace_zeroed, st), f"e2e {n}")
+                continue
+            if tp and n in ROW_PARALLEL and peers is not None:
+                check(lib.grinqh_gemm_allreduce(xp, GRINQH_BF16, M, K, w.data_ptr(), s.data_ptr(), None, bits, GROUP,
+                                                N, th_args[n], MODE_AUTO | workspace_zeroed, yp, ws.data_ptr(),
+                                                ws.numel(), peers.rank, peers.world, bufs, peers.n_cap, st),
+                      f"e2e {n}")
                 continue
             check(lib.grinqh_gemm_or_gemv(xp, GRINQH_BF16, M, K, w.data_ptr(), s.data_ptr(), None, bits, GROUP, N,
                                           th_args[n], MODE_AUTO | workspace_zeroed, yp, ws.data_ptr(), ws.numel(), st),
@@ -708,19 +723,64 @@ def run_reference(args):
     }
 
 
+def run_only(args, dev):
+    """One linear at --m rows (--graded: per-token graded, else the AUTO dispatch), called
+    --warmup times and then --steps times eagerly on one GPU, two weight copies rotated
+    (inputs larger than L2 between calls for the wide shapes). A short, fixed launch
+    sequence for profiler captures (ncu -k ... -s <warmup> -c <n>); prints us per call."""
+    from grinqh.kernel import grinqh_gemm_or_gemv
+    from grinqh.utils import pack_codes
+    name, bits, M = args.only, args.bits, args.m
+    K, N = SHAPES[name]
+    copies = []
+    for seed in range(2):
+        codes, s_ = make_codes(dev, bits, seed, name)
+        copies.append((pack_codes(codes, bits), s_))
+        del codes
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    th = torch.quantile(x.abs().float().flatten()[: 1 << 24], torch.tensor(QUANTILES, device=dev)).tolist()
+
+    def call(i):
+        w, s_ = copies[i % 2]
+        if args.graded:
+            return torch.ops.grinqh.linear(x, w, s_, None, bits, GROUP, N // 4, th, 2)
+        return grinqh_gemm_or_gemv(x, w, s_, None, bits, GROUP, N // 4, th)
+
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(args.steps):
+        call(i)
+    b.record()
+    torch.cuda.synchronize(dev)
+    us = a.elapsed_time(b) * 1e3 / max(args.steps, 1)
+    return {"only": name, "M": M, "bits": bits, "graded": bool(args.graded), "us_per_call": round(us, 2),
+            "note": "eager calls for profiler captures; not a bench line"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--m", type=int, default=1, help="decode batch rows per linear")
+    ap.add_argument("--m", "--rows", dest="m", type=int, default=1,
+                    help="decode batch rows per linear (--rows under torchrun, which claims --m)")
     ap.add_argument("--bits", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the M = 16..8192 sweep of configs[1]")
     ap.add_argument("--replicas", action="store_true",
                     help="with several GPUs: independent replicas instead of the tensor-parallel layer")
+    ap.add_argument("--only", choices=list(SHAPES), default=None,
+                    help="profiling: call one linear at --m rows, --warmup then --steps times, and exit")
+    ap.add_argument("--graded", action="store_true", help="with --only: per-token graded rows (mode 2)")
     args = ap.parse_args()
+    if args.only:
+        print(json.dumps(run_only(args, torch.device("cuda", 0))), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

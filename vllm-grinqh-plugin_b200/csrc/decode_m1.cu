@@ -19,6 +19,10 @@
 // fixed order, so results are deterministic.
 #include <cooperative_groups.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "decode_m1.cuh"
 #include "ptx.cuh"
@@ -389,14 +393,10 @@ bool m1_supported(int64_t M, int64_t K, int64_t N, int group) {
   return M == 1 && N % 32 == 0 && K % group == 0 && group % kD == 0;
 }
 
-M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
+static M1Plan plan_for(int64_t K, int64_t N, int64_t target) {
   M1Plan p{};
   const int64_t n16 = N / 16;
   p.tiles = (int)((n16 + kSliceW - 1) / kSliceW);
-  // one wave: 2 CTAs fit per SM, but 8-CTA clusters pack into the GPCs less densely;
-  // a target of 1.9 CTAs per SM measured best on a 148-SM B200 (K = 14336: 22.3 us
-  // against 23.7 us at 1.7; the other Llama shapes unchanged)
-  const int64_t target = (sm_count > 0 ? sm_count : 148) * 19 / 10;
   int64_t splits = target / p.tiles;
   const int64_t max_splits = (K + kWarps * kD - 1) / (kWarps * kD);
   if (splits > max_splits) splits = max_splits;
@@ -413,8 +413,69 @@ M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
   p.slot_bytes = nclu > 1 ? (size_t)p.tiles * nclu * kSliceN * sizeof(float) : 0;
   p.counter_bytes = nclu > 1 ? (size_t)p.tiles * sizeof(unsigned) : 0;
   p.smem_bytes = m1_meta_bytes(p.rows_per_cta) + (kWarps + 1) * kSliceN * sizeof(float);
-  (void)group;
   return p;
+}
+
+// Clusters of `cluster` CTAs with `smem` bytes of dynamic shared memory each that the
+// current device holds at once; 0 if no device can be asked. Every instantiation of
+// the kernel has the same block size and register bound, so one answers for all.
+static int resident_clusters(int cluster, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(dev, cluster, smem);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto kern = m1_kernel<4, __nv_bfloat16, false>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, (unsigned)cluster, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)cluster;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
+  // One wave: 2 CTAs fit per SM, and a target of 1.9 CTAs per SM measured best on a
+  // 148-SM B200. Clusters live inside one GPC, so 8-CTA clusters do not tile all SMs:
+  // a grid with more clusters than the device holds at once would run the rest as a
+  // second wave (and the fused all-reduce launch needs every CTA running), so the split
+  // count drops one cluster per tile at a time until the grid is resident. Without a
+  // device to ask (host-only queries) the first plan stands.
+  (void)group;
+  int64_t target = (int64_t)(sm_count > 0 ? sm_count : 148) * 19 / 10;
+  M1Plan p = plan_for(K, N, target);
+  for (;;) {
+    const int have = resident_clusters(p.cluster, p.smem_bytes);
+    if (have <= 0 || (int64_t)p.tiles * p.grid_splits <= (int64_t)have * p.cluster) return p;
+    if (p.grid_splits <= p.cluster) return p;  // one cluster per tile is the least
+    target = (int64_t)p.tiles * (p.grid_splits - p.cluster);
+    const M1Plan q = plan_for(K, N, target);
+    if ((int64_t)q.tiles * q.grid_splits >= (int64_t)p.tiles * p.grid_splits) return p;
+    p = q;
+  }
 }
 
 template <bool kAR>

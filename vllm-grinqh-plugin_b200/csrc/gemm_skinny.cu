@@ -577,11 +577,6 @@ static SkinnyPlan plan_for(int64_t M, int64_t K, int64_t N, int64_t target, int 
   return p;
 }
 
-SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
-  // one CTA per SM (about 200 KB of shared memory each); clusters of up to 8 pack
-  // into the GPCs less densely than single CTAs, so aim a little under the SM count
-  return plan_for(M, K, N, (int64_t)(sm_count > 0 ? sm_count : 148) * 7 / 8);
-}
 
 // Clusters of `cluster` CTAs that the current device holds at once. Every
 // instantiation of the kernel has the same block size, shared memory and register
@@ -654,6 +649,17 @@ static int launch_ar(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz
     case 3: return launch_t<3, __half, kAR>(a, p, st);
     default: return launch_t<4, __half, kAR>(a, p, st);
   }
+}
+
+SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count) {
+  // One CTA per SM (about 225 KB of shared memory each), aiming a little under the SM
+  // count. Clusters live inside one GPC, so 8-CTA clusters do not tile all SMs (a
+  // 148-SM B200 holds 15 of them, 120 CTAs): a grid one cluster too large would run
+  // that cluster as a second wave, doubling the time. The resident plan avoids that;
+  // without a device to ask (host-only queries) the plain plan is used.
+  SkinnyPlan p{};
+  if (plan_skinny_resident(M, K, N, sm_count, &p)) return p;
+  return plan_for(M, K, N, (int64_t)(sm_count > 0 ? sm_count : 148) * 7 / 8);
 }
 
 int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st, bool allreduce) {

@@ -31,11 +31,14 @@ struct SkinnyPlan {
 
 bool skinny_supported(int64_t M, int64_t K, int64_t N, int group);
 bool skinny_pointers_ok(const void* x, const void* w, const void* s);
-SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count);
-// The plan of the fused all-reduce launch: as plan_skinny, with fewer K splits where
-// needed so that the whole grid is resident at once (its CTAs wait on the peer ranks'
-// CTAs, which must all be running). False if no plan is.
+// A plan whose whole grid is resident at once (smaller clusters or fewer K splits
+// where the default does not fit); false if none is, or no device can be asked. The
+// fused all-reduce launch requires it: its CTAs wait on the peer ranks' CTAs, which
+// must all be running.
 bool plan_skinny_resident(int64_t M, int64_t K, int64_t N, int sm_count, SkinnyPlan* out);
+// The launch plan: the resident plan where there is one (a grid one cluster too large
+// would run that cluster as a second wave), else the default.
+SkinnyPlan plan_skinny(int64_t M, int64_t K, int64_t N, int sm_count);
 int launch_skinny(const SkinnyArgs& a, const SkinnyPlan& p, int dtype, int nz, cudaStream_t st,
                   bool allreduce = false);
 unsigned take_skinny_timeouts();
