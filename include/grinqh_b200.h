@@ -20,6 +20,9 @@
  *   grinqh_gemm_or_gemv      <- grinqh/kernel.py:646-710 torch.ops.grinqh.gemm_or_gemv
  *   grinqh_gemv_batch_union  <- grinqh/kernel.py:607-643 grinqh_gemv_batch_union
  *   grinqh_prefill_gemm      <- grinqh/kernel.py:561-587 grinqh_prefill_gemm_compiled
+ *   grinqh_rmsnorm_grade, grinqh_silu_mul_grade, grinqh_gemv_batch_union_masked
+ *                            <- the grading of kernel.py:100-116 moved into the producer of x
+ *                               (vLLM's RMSNorm / SiluAndMul, which precede qkv, gate_up, down)
  *
  * Tensor layouts (row-major, contiguous unless a leading dimension is given):
  *   x              [M, K]            activations, dtype (bf16 or fp16)
@@ -146,6 +149,36 @@ int grinqh_gemv_batch_union(const void *x_dev, int dtype, int64_t M, int64_t K,
                             const void *bias_dev, int max_bits, int group_size, int64_t N,
                             const float *thresholds, void *y_dev, void *workspace_dev,
                             size_t workspace_bytes, grinqh_stream_t stream);
+
+/* grinqh_gemv_batch_union with the rows' union of grades supplied (union_mask_dev [K]
+ * uint8, from grinqh_rmsnorm_grade / grinqh_silu_mul_grade or grinqh_grade on the same
+ * x and thresholds) instead of graded again from every row of x inside the GEMV. */
+int grinqh_gemv_batch_union_masked(const void *x_dev, int dtype, int64_t M, int64_t K,
+                                   const uint32_t *weight_packed_dev, const void *weight_scale_dev,
+                                   const void *bias_dev, int max_bits, int group_size, int64_t N,
+                                   const float *thresholds, const uint8_t *union_mask_dev, void *y_dev,
+                                   void *workspace_dev, size_t workspace_bytes, grinqh_stream_t stream);
+
+/* ---- Producers of x with the grading fused in (no counterpart in the reference,
+ * which grades inside its GEMV, grinqh/kernel.py:100-116, or in a separate pass over x).
+ * Each writes x for the next linear, its grade masks (masks_dev [M, K], as grinqh_grade;
+ * NULL: not written) and their union over the rows (union_dev [K], cleared on the
+ * stream first; NULL: not written), graded from the written (rounded) values.
+ * thresholds: 4 host floats (may be NULL when neither mask is asked for). K % 8 == 0;
+ * x, residual, weight and out 16-byte aligned, masks 8-byte, union 4-byte.
+ *   grinqh_rmsnorm_grade: vLLM's rms_norm / fused_add_rms_norm
+ *     (vllm/ir/ops/layernorm.py:10-58): s = x (+ residual; residual_dev, if not NULL,
+ *     is replaced by dtype(s)); out = dtype(dtype(s * rsqrt(mean(s^2) + eps)) * weight)
+ *     (weight_dev NULL: no weight). x and out [M, K]; K * 4 bytes must fit in shared
+ *     memory (K <= 58112).
+ *   grinqh_silu_mul_grade: vLLM's SiluAndMul on x_dev [M, 2K] = [gate | up]:
+ *     out [M, K] = dtype(dtype(gate / (1 + exp(-gate))) * up). */
+int grinqh_rmsnorm_grade(const void *x_dev, void *residual_dev, const void *weight_dev, int dtype, int64_t M,
+                         int64_t K, float eps, const float *thresholds, int max_bits, void *out_dev,
+                         uint8_t *masks_dev, uint8_t *union_dev, grinqh_stream_t stream);
+int grinqh_silu_mul_grade(const void *x_dev, int dtype, int64_t M, int64_t K, const float *thresholds,
+                          int max_bits, void *out_dev, uint8_t *masks_dev, uint8_t *union_dev,
+                          grinqh_stream_t stream);
 
 /* Dense path y = x @ dtype(w * s) for any M >= 1 (grinqh/kernel.py:561-587); same as
  * grinqh_gemm_or_gemv with mode = GRINQH_MODE_DENSE. */

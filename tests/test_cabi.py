@@ -63,7 +63,8 @@ def test_calls_without_gpu_fail_loudly():
 def test_torch_ops_registered():
     import torch
     import grinqh.kernel  # noqa: F401
-    for name in ("gemm_or_gemv", "linear", "pack", "pack_codes", "unpack", "grade"):
+    for name in ("gemm_or_gemv", "linear", "pack", "pack_codes", "unpack", "grade", "rmsnorm_grade",
+                 "silu_mul_grade", "union_linear_masked", "linear_allreduce", "gemv_allreduce"):
         assert hasattr(torch.ops.grinqh, name)
     schema = str(torch.ops.grinqh.gemm_or_gemv.default._schema)
     assert "float[] thresholds" in schema and "bool use_marlin=False" in schema
@@ -90,3 +91,9 @@ def test_fake_impl_shapes():
         s = torch.empty(2, 320, dtype=torch.bfloat16, device="cuda")
         y = torch.ops.grinqh.gemm_or_gemv(x, w, s, None, 8, 128, 80, [0.1, 0.2, 0.3, 0.4])
         assert tuple(y.shape) == (3, 5, 320) and y.dtype == torch.bfloat16
+        o, m, u = torch.ops.grinqh.rmsnorm_grade(x, None, None, 1e-5, [0.1] * 4, 8)
+        assert tuple(o.shape) == (3, 5, 256) and tuple(m.shape) == (3, 5, 256) and tuple(u.shape) == (256,)
+        o, m, u = torch.ops.grinqh.silu_mul_grade(x, [0.1] * 4, 8)
+        assert tuple(o.shape) == (3, 5, 128) and m.dtype == torch.uint8 and tuple(u.shape) == (128,)
+        y = torch.ops.grinqh.union_linear_masked(x, w, s, None, 8, 128, 80, [0.1] * 4, u)
+        assert tuple(y.shape) == (3, 5, 320)

@@ -255,10 +255,12 @@ extern "C" size_t grinqh_workspace_size(int64_t M, int64_t K, int64_t N, int max
   return generic;
 }
 
-extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
-                                   const void* s, const void* bias, int max_bits, int group, int64_t N,
-                                   const float* thresholds, int mode, void* y, void* workspace,
-                                   size_t workspace_bytes, grinqh_stream_t stream) {
+// umask: the rows' union of grades per k, from a producer that graded x as it wrote it
+// (union mode with several rows; null: the kernel grades x itself).
+static int gemm_or_gemv_impl(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w, const void* s,
+                             const void* bias, int max_bits, int group, int64_t N, const float* thresholds, int mode,
+                             void* y, void* workspace, size_t workspace_bytes, const uint8_t* umask,
+                             grinqh_stream_t stream) {
   int dev = 0, sms = 0;
   GRINQH_RETURN_IF(device_info(&dev, &sms));
   GRINQH_RETURN_IF(validate(x, dtype, M, K, w, s, max_bits, group, N, y));
@@ -425,10 +427,28 @@ extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t 
   a.rows_per_cta = plan.rows_per_cta;
   a.ksplit = plan.ksplit;
   for (int z = 0; z < 4; ++z) a.t[z] = thresholds ? thresholds[z] : 0.0f;
+  a.umask = km == kModeUnion ? umask : nullptr;
   if (plan.ksplit > 1)
     GRINQH_RETURN_IF(bind_workspace(workspace, plan.partial_bytes, plan.counter_bytes, zeroed, stream, &a.partial,
                                     &a.counters));
   return launch_decode(a, plan, km, dtype, max_bits / 2, stream);
+}
+
+extern "C" int grinqh_gemm_or_gemv(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                   const void* s, const void* bias, int max_bits, int group, int64_t N,
+                                   const float* thresholds, int mode, void* y, void* workspace,
+                                   size_t workspace_bytes, grinqh_stream_t stream) {
+  return gemm_or_gemv_impl(x, dtype, M, K, w, s, bias, max_bits, group, N, thresholds, mode, y, workspace,
+                           workspace_bytes, nullptr, stream);
+}
+
+extern "C" int grinqh_gemv_batch_union_masked(const void* x, int dtype, int64_t M, int64_t K, const uint32_t* w,
+                                              const void* s, const void* bias, int max_bits, int group, int64_t N,
+                                              const float* thresholds, const uint8_t* union_mask, void* y,
+                                              void* workspace, size_t workspace_bytes, grinqh_stream_t stream) {
+  GRINQH_REQUIRE(union_mask, "union_mask required");
+  return gemm_or_gemv_impl(x, dtype, M, K, w, s, bias, max_bits, group, N, thresholds, GRINQH_MODE_UNION, y,
+                           workspace, workspace_bytes, union_mask, stream);
 }
 
 // ---------------------------------------------------------------- fused all-reduce

@@ -66,8 +66,12 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeArgs a) {
   for (int r = threadIdx.x; r < R; r += kThreads) {
     const int k = k0 + r;
     uint32_t um = (MODE == kModeDense) ? ((1u << NZ) - 1u) : 0u;
-    if (MODE == kModeUnion)
-      for (int m = 0; m < a.M; ++m) um |= grade_bits<NZ>(Act<T>::to_f(x[(size_t)m * a.K + k]), a);
+    if (MODE == kModeUnion) {
+      if (a.umask)  // graded by the producer of x (produce.cu)
+        um = a.umask[k] & ((1u << NZ) - 1u);
+      else
+        for (int m = 0; m < a.M; ++m) um |= grade_bits<NZ>(Act<T>::to_f(x[(size_t)m * a.K + k]), a);
+    }
 #pragma unroll
     for (int mm = 0; mm < MT; ++mm) {
       const int m = m0 + mm;

@@ -21,6 +21,7 @@ struct DecodeArgs {
   unsigned* counters;   // [chunks, jtiles] tickets, zero before launch
   int M, K, N, group, rows_per_cta, ksplit;
   float t[4];
+  const uint8_t* umask;  // [K] union of the rows' grades (union mode), or null: graded here
 };
 
 struct DecodePlan {

@@ -101,7 +101,8 @@ int env_mode_for_rows() {
 
 at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
                       const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
-                      int64_t original_n, at::ArrayRef<double> thresholds, int mode) {
+                      int64_t original_n, at::ArrayRef<double> thresholds, int mode,
+                      const at::Tensor* union_mask = nullptr) {
   const NvtxRange range("grinqh::linear");
   check_cuda(x, "x");
   check_cuda(weight_packed, "weight_packed");
@@ -143,6 +144,18 @@ at::Tensor run_linear(const at::Tensor& x, const at::Tensor& weight_packed, cons
   bool zeroed = false;
   if (ws_bytes) ws = stream_workspace(x, ws_bytes, stream, &zeroed);
   const int call_mode = zeroed ? (mode | GRINQH_WORKSPACE_ZEROED) : mode;
+  if (union_mask) {  // the rows' union of grades from the producer of x
+    check_cuda(*union_mask, "union_mask");
+    TORCH_CHECK(union_mask->scalar_type() == at::kByte && union_mask->numel() == K && union_mask->is_contiguous(),
+                "GRINQH: union_mask must be a contiguous uint8 tensor of K values");
+    check_ok(grinqh_gemv_batch_union_masked(
+                 xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()), sc.data_ptr(),
+                 bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N, th.data(),
+                 union_mask->data_ptr<uint8_t>(), y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr,
+                 ws_bytes ? static_cast<size_t>(ws.numel()) : 0, stream),
+             "gemv_batch_union_masked");
+    return y.view(out_shape);
+  }
   const int st = grinqh_gemm_or_gemv(xf.data_ptr(), dt, M, K, reinterpret_cast<const uint32_t*>(wp.data_ptr()),
                                      sc.data_ptr(), bias ? bc.data_ptr() : nullptr, (int)max_bits, (int)group_size, N,
                                      th.data(), call_mode, y.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr,
@@ -270,6 +283,75 @@ at::Tensor linear(const at::Tensor& x, const at::Tensor& weight_packed, const at
   return run_linear(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds, (int)mode);
 }
 
+// The batch-union GEMV with the union of grades from the producer of x (rmsnorm_grade /
+// silu_mul_grade), which the kernel then does not recompute from every row of x.
+at::Tensor union_linear_masked(const at::Tensor& x, const at::Tensor& weight_packed, const at::Tensor& weight_scale,
+                               const std::optional<at::Tensor>& bias, int64_t max_bits, int64_t group_size,
+                               int64_t original_n, at::ArrayRef<double> thresholds, const at::Tensor& union_mask) {
+  return run_linear(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds,
+                    GRINQH_MODE_UNION, &union_mask);
+}
+
+// x for the next linear together with its grades (C ABI grinqh_rmsnorm_grade): returns
+// (out, masks [M, K] uint8, union [K] uint8); residual, if given, is updated in place
+// to dtype(x + residual) as vLLM's fused_add_rms_norm does.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> rmsnorm_grade(const at::Tensor& x,
+                                                             const std::optional<at::Tensor>& residual,
+                                                             const std::optional<at::Tensor>& weight, double eps,
+                                                             at::ArrayRef<double> thresholds, int64_t max_bits) {
+  const NvtxRange range("grinqh::rmsnorm_grade");
+  check_cuda(x, "x");
+  const int dt = dtype_code(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "GRINQH rmsnorm_grade: x must be contiguous");
+  const int64_t K = x.size(-1), M = K ? x.numel() / K : 0;
+  if (residual) {
+    check_cuda(*residual, "residual");
+    TORCH_CHECK(residual->scalar_type() == x.scalar_type() && residual->sizes() == x.sizes() &&
+                    residual->is_contiguous(),
+                "GRINQH rmsnorm_grade: residual must be a contiguous tensor like x");
+  }
+  at::Tensor wc;
+  if (weight) {
+    check_cuda(*weight, "weight");
+    TORCH_CHECK(weight->scalar_type() == x.scalar_type() && weight->numel() == K,
+                "GRINQH rmsnorm_grade: weight must be [K] of x's dtype");
+    wc = weight->contiguous();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty_like(x);
+  at::Tensor masks = at::empty({M, K}, x.options().dtype(at::kByte));
+  at::Tensor uni = at::empty({K}, x.options().dtype(at::kByte));
+  const auto th = thresholds4(thresholds);
+  check_ok(grinqh_rmsnorm_grade(x.data_ptr(), residual ? residual->data_ptr() : nullptr,
+                                weight ? wc.data_ptr() : nullptr, dt, M, K, (float)eps, th.data(), (int)max_bits,
+                                out.data_ptr(), masks.data_ptr<uint8_t>(), uni.data_ptr<uint8_t>(), cur_stream(x)),
+           "rmsnorm_grade");
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  return {out, masks.view(shape), uni};
+}
+
+// silu(gate) * up of x = [..., 2K] with its grades (C ABI grinqh_silu_mul_grade).
+std::tuple<at::Tensor, at::Tensor, at::Tensor> silu_mul_grade(const at::Tensor& x, at::ArrayRef<double> thresholds,
+                                                              int64_t max_bits) {
+  const NvtxRange range("grinqh::silu_mul_grade");
+  check_cuda(x, "x");
+  const int dt = dtype_code(x, "x");
+  TORCH_CHECK(x.size(-1) % 2 == 0, "GRINQH silu_mul_grade: the last dimension must be even");
+  const at::Tensor xc = x.contiguous();
+  const int64_t K = x.size(-1) / 2, M = K ? x.numel() / (2 * K) : 0;
+  const c10::cuda::CUDAGuard guard(x.device());
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  shape.back() = K;
+  at::Tensor out = at::empty(shape, x.options());
+  at::Tensor masks = at::empty(shape, x.options().dtype(at::kByte));
+  at::Tensor uni = at::empty({K}, x.options().dtype(at::kByte));
+  const auto th = thresholds4(thresholds);
+  check_ok(grinqh_silu_mul_grade(xc.data_ptr(), dt, M, K, th.data(), (int)max_bits, out.data_ptr(),
+                                 masks.data_ptr<uint8_t>(), uni.data_ptr<uint8_t>(), cur_stream(x)),
+           "silu_mul_grade");
+  return {out, masks, uni};
+}
+
 // pack_triton (grinqh/utils.py:125-146): [K, N/4] shifted code words -> [K, (b/2)*N/16]
 at::Tensor pack(const at::Tensor& words, int64_t max_bits) {
   check_cuda(words, "words");
@@ -372,6 +454,11 @@ TORCH_LIBRARY(grinqh, m) {
         "int group_size, int original_n, float[] thresholds, int mode, int rank, int world, int[] buffers, "
         "int cap) -> Tensor");
   m.def("grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor)");
+  m.def("rmsnorm_grade(Tensor x, Tensor(a!)? residual, Tensor? weight, float eps, float[] thresholds, "
+        "int max_bits) -> (Tensor, Tensor, Tensor)");
+  m.def("silu_mul_grade(Tensor x, float[] thresholds, int max_bits) -> (Tensor, Tensor, Tensor)");
+  m.def("union_linear_masked(Tensor x, Tensor weight_packed, Tensor weight_scale, Tensor? bias, int max_bits, "
+        "int group_size, int original_n, float[] thresholds, Tensor union_mask) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
@@ -384,4 +471,7 @@ TORCH_LIBRARY_IMPL(grinqh, CUDA, m) {
   m.impl("gemv_allreduce", &gemv_allreduce);
   m.impl("linear_allreduce", &linear_allreduce);
   m.impl("grade", &grade);
+  m.impl("rmsnorm_grade", &rmsnorm_grade);
+  m.impl("silu_mul_grade", &silu_mul_grade);
+  m.impl("union_linear_masked", &union_linear_masked);
 }

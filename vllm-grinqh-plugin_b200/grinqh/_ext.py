@@ -51,6 +51,11 @@ SIGNATURES = {
                                        _ptr, _ptr, _size, _ptr]),
     "grinqh_prefill_gemm": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _ptr, _ptr,
                                    _size, _ptr]),
+    "grinqh_gemv_batch_union_masked": (_int, [_ptr, _int, _i64, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr,
+                                              _ptr, _ptr, _ptr, _size, _ptr]),
+    "grinqh_rmsnorm_grade": (_int, [_ptr, _ptr, _ptr, _int, _i64, _i64, ctypes.c_float, _fptr, _int, _ptr, _ptr,
+                                    _ptr, _ptr]),
+    "grinqh_silu_mul_grade": (_int, [_ptr, _int, _i64, _i64, _fptr, _int, _ptr, _ptr, _ptr, _ptr]),
     "grinqh_gemv_noalloc": (_int, [_ptr, _int, _i64, _ptr, _ptr, _ptr, _int, _int, _i64, _fptr, _ptr, _ptr]),
 }
 

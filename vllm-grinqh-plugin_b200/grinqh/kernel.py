@@ -18,7 +18,8 @@ load_ops()
 
 __all__ = [
     "grinqh_gemm_or_gemv", "grinqh_linear", "grinqh_prefill_gemm_compiled", "grinqh_prefill_gemm",
-    "grinqh_gemv_batch_union", "grinqh_prefill_marlin", "grinqh_grade",
+    "grinqh_gemv_batch_union", "grinqh_prefill_marlin", "grinqh_grade", "grinqh_rmsnorm_grade",
+    "grinqh_silu_mul_grade", "grinqh_gemv_batch_union_masked",
     "MODE_AUTO", "MODE_DENSE", "MODE_GRADED", "MODE_UNION",
 ]
 
@@ -76,6 +77,24 @@ def _fake_grade(x, thresholds, max_bits):
     return x.new_empty(x.shape, dtype=torch.uint8), x.new_empty((x.shape[-1],), dtype=torch.uint8)
 
 
+@torch.library.register_fake("grinqh::rmsnorm_grade")
+def _fake_rmsnorm_grade(x, residual, weight, eps, thresholds, max_bits):
+    return (torch.empty_like(x), x.new_empty(x.shape, dtype=torch.uint8),
+            x.new_empty((x.shape[-1],), dtype=torch.uint8))
+
+
+@torch.library.register_fake("grinqh::silu_mul_grade")
+def _fake_silu_mul_grade(x, thresholds, max_bits):
+    shape = (*x.shape[:-1], x.shape[-1] // 2)
+    return x.new_empty(shape), x.new_empty(shape, dtype=torch.uint8), x.new_empty((shape[-1],), dtype=torch.uint8)
+
+
+@torch.library.register_fake("grinqh::union_linear_masked")
+def _fake_union_linear_masked(x, weight_packed, weight_scale, bias, max_bits, group_size, original_n, thresholds,
+                              union_mask):
+    return x.new_empty((*x.shape[:-1], 4 * original_n))
+
+
 def grinqh_gemm_or_gemv(x: torch.Tensor, weight_packed: torch.Tensor, weight_scale: torch.Tensor,
                         bias: Optional[torch.Tensor], max_bits: int, group_size: int, original_n: int,
                         thresholds: List[float], use_marlin: bool = False) -> torch.Tensor:
@@ -123,3 +142,24 @@ def grinqh_gemv_batch_union(x: torch.Tensor, weight_packed: torch.Tensor, weight
 def grinqh_grade(x: torch.Tensor, thresholds: List[float], max_bits: int):
     """Per-element zone masks (bit z: fp32|x| > t_z) and their union over rows."""
     return torch.ops.grinqh.grade(x, [float(t) for t in thresholds], max_bits)
+
+
+def grinqh_rmsnorm_grade(x: torch.Tensor, residual: Optional[torch.Tensor], weight: Optional[torch.Tensor],
+                         eps: float, thresholds: List[float], max_bits: int):
+    """vLLM's RMSNorm (with the residual add when ``residual`` is given, updated in place)
+    producing x for the next linear together with its grade masks and their union over
+    rows: (out, masks, union)."""
+    return torch.ops.grinqh.rmsnorm_grade(x, residual, weight, float(eps), [float(t) for t in thresholds], max_bits)
+
+
+def grinqh_silu_mul_grade(x: torch.Tensor, thresholds: List[float], max_bits: int):
+    """vLLM's SiluAndMul on x = [gate | up] with the grades of the product: (out, masks, union)."""
+    return torch.ops.grinqh.silu_mul_grade(x, [float(t) for t in thresholds], max_bits)
+
+
+def grinqh_gemv_batch_union_masked(x: torch.Tensor, weight_packed: torch.Tensor, weight_scale: torch.Tensor,
+                                   bias: Optional[torch.Tensor], max_bits: int, group_size: int, original_n: int,
+                                   thresholds: List[float], union_mask: torch.Tensor) -> torch.Tensor:
+    """grinqh_gemv_batch_union with the union of grades from the producer of x."""
+    return torch.ops.grinqh.union_linear_masked(x, weight_packed, weight_scale, bias, max_bits, group_size,
+                                                original_n, [float(t) for t in thresholds], union_mask)
