@@ -8,19 +8,21 @@
 // of 32 rows. Three rings of shared-memory stages:
 //   planes  (5 x 16 KB)  the b/2 plane words of 32 rows x 32 words, one 2-D TMA box
 //                        per plane (128-byte swizzle), loaded up to five steps ahead
-//                        by warp 8;
+//                        by the loader warp;
 //   weights (4 x 32 KB)  operand A: dtype(w * s) for 512 columns x 32 rows, MN-major
 //                        with the 128-byte swizzle;
 //   x       (4 x 4 KB)   operand B: Mp x 32 activations, K-major with the 64-byte
 //                        swizzle (rows past M read as 0), loaded by TMA.
-// Warps 0-7 convert (a warp covers 8 rows x 4 word pairs twice, so that every
+// Warps 0-15 convert (a warp covers 8 rows x 4 word pairs, so that every
 // shared-memory access is free of bank conflicts): each thread owns two neighbouring
-// words of two rows 8 apart (same columns, same scales), reads their
-// planes from shared memory, merges them into codes, multiplies by the group scale,
-// rounds once to the activation dtype -- the reference's dtype(w * s), bit for bit --
-// and stores the weight stage. Warp 9 issues the MMAs (per 16-deep K slice, one
+// words of one row (same scales' rows), reads their planes from shared memory, merges
+// them into codes, forms the exact code in fp32, packs it to the activation dtype
+// (exact: |code| <= 128) and multiplies it by the packed scale pair with one rounding
+// -- the reference's dtype(w * s), bit for bit -- and stores the weight stage. Four
+// converter warps per scheduler (96 registers a thread) hide the latency of that
+// chain. Warp 16 loads the planes; warp 17 issues the MMAs (per 16-deep K slice, one
 // tcgen05.mma kind::f16 per 128-column block, N = Mp) from one thread into TMEM;
-// tcgen05.commit frees the stage, and a second lane of warp 9 then loads the x tile
+// tcgen05.commit frees the stage, and a second lane of warp 17 then loads the x tile
 // of the step that reuses it (the x loads stay off the plane loader's TMA queue and
 // out of the converters' loop). The converters never wait on global memory: the
 // plane ring hides its latency.
@@ -58,8 +60,13 @@ constexpr int TW = 32;         // packed words per tile
 constexpr int TN = 16 * TW;    // output columns per tile
 constexpr int BK = 32;         // rows per K step
 constexpr int SP = 5, SW = 4;  // plane stages; weight / activation stages
-constexpr int kConvWarps = 8;
-constexpr int kLoadWarp = 8, kMmaWarp = 9;
+#ifndef GRINQH_SKINNY_CONV_WARPS
+#define GRINQH_SKINNY_CONV_WARPS 16
+#endif
+constexpr int kConvWarps = GRINQH_SKINNY_CONV_WARPS;  // 8 (two rows a thread) or 16 (one row)
+static_assert(kConvWarps == 8 || kConvWarps == 16, "converter warps");
+constexpr int kRowsPerThread = 16 / kConvWarps;       // rows of a step per converter thread
+constexpr int kLoadWarp = kConvWarps, kMmaWarp = kConvWarps + 1;
 constexpr int kThreads = 32 * (kConvWarps + 2);
 constexpr int kMaxMp = 64;
 constexpr uint32_t kPlaneBytes = BK * TW * 4;  // one plane of a step: 4 KB
@@ -88,6 +95,12 @@ template <> struct Fmt<__nv_bfloat16> {
   static __device__ __forceinline__ float2 unpack(uint32_t bits) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bits));
   }
+  // a * b per half, rounded once to the dtype (the exact product of two dtype values)
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
 };
 template <> struct Fmt<__half> {
   static constexpr uint32_t v = 0;
@@ -97,6 +110,11 @@ template <> struct Fmt<__half> {
   }
   static __device__ __forceinline__ float2 unpack(uint32_t bits) {
     return __half22float2(*reinterpret_cast<const __half2*>(&bits));
+  }
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
   }
 };
 
@@ -213,23 +231,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ converters
-    // a warp covers 8 rows x 4 word pairs, twice: in every shared-memory access the 8
-    // lanes of a phase are 8 different rows, which the 128-byte swizzle spreads over
-    // all banks
-    const int rr = 16 * (warp & 1) + (lane & 7);     // rows rr and rr + 8 of each step
-    const int jp = 4 * (warp >> 1) + (lane >> 3);    // this thread's words: 2 jp, 2 jp + 1
+    // a warp covers 8 rows x 4 word pairs (kRowsPerThread times): in every
+    // shared-memory access the 8 lanes of a phase are 8 different rows, which the
+    // 128-byte swizzle spreads over all banks
+    constexpr int kWarpRowSets = 4 / kRowsPerThread;          // warps side by side along the rows
+    const int rr = 8 * kRowsPerThread * (warp % kWarpRowSets) + (lane & 7);  // rows rr + 8 h
+    const int jp = 4 * (warp / kWarpRowSets) + (lane >> 3);   // this thread's words: 2 jp, 2 jp + 1
     const int jw = jt0 + 2 * jp;
     const bool jvalid = jw < n16;      // n16 is even: both words are valid or neither
     const int spg = a.group / BK;      // K steps per scale group
     // byte u (offset binary, code = u - 128, shifted left by 8 - b) -> u / 2^shift plus
-    // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u
+    // 2^(23-shift), exactly: the float with bits 0x4B000000 - (shift << 23) | u; minus
+    // the magic constant that is the unshifted code, exactly
     constexpr uint32_t kMagicBits = 0x4B000000u - ((uint32_t)kShift << 23);
     constexpr float kMagic = (float)(8388608.0 + 128.0) / float(1 << kShift);
-    // scales of column group c for the two words, s[g, c * n16 + jw .. jw + 1] (the
-    // 2^-shift of the shifted codes is in the magic constant below); the next group's
-    // are prefetched as packed dtype pairs
-    float2 sreg[16], sneg[16];  // s and -(2^23 + 128) * s / 2^shift per column group
-    uint32_t snext[16];
+    // Scales of the current group as packed dtype pairs of neighbouring column groups:
+    // sa[2t + p] = (s[4t + 2p], s[4t + 2p + 1]) of word 2 jp, sb the same of word
+    // 2 jp + 1, where s[c] = s[g, c * n16 + word]. The next group's scales are
+    // prefetched as they lie in memory (snext[c] = both words of column group c).
+    uint32_t sa[8], sb[8], snext[16];
     auto load_scales = [&](int g) {
       const uint32_t* sp =
           reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.s) + (size_t)g * a.N + (jvalid ? jw : 0));
@@ -238,47 +258,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     auto unpack_scales = [&]() {
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        sreg[c] = Fmt<T>::unpack(snext[c]);
-        sneg[c] = make_float2(-kMagic * sreg[c].x, -kMagic * sreg[c].y);
+      for (int k = 0; k < 8; ++k) {
+        sa[k] = __byte_perm(snext[2 * k], snext[2 * k + 1], 0x5410u);
+        sb[k] = __byte_perm(snext[2 * k], snext[2 * k + 1], 0x7632u);
       }
     };
+    int g_next = 0;  // first K step of the next scale group
     if (nq > 0) {
       const int g0 = q0 / spg;
       load_scales(g0);
       unpack_scales();
-      if ((g0 + 1) * spg < q0 + nq) load_scales(g0 + 1);
+      g_next = (g0 + 1) * spg;
+      if (g_next < q0 + nq) load_scales(g0 + 1);
     }
-    // store offsets of rows rr, rr + 8 in the weight stage (MN-major, 128-byte swizzle:
-    // 16-byte chunk c of row k sits at (c ^ (k & 7)); both rows have k & 7 = rr & 7)
+    // store offsets of rows rr + 8 h in the weight stage (MN-major, 128-byte swizzle:
+    // 16-byte chunk c of row k sits at (c ^ (k & 7)); every row has k & 7 = rr & 7)
     const uint32_t rsw = (uint32_t)(rr & 7);
     const uint32_t c0 = (uint32_t)(4 * jp) & 7u;  // first of the thread's four chunks (0 or 4)
-    uint32_t row_base[2];
+    uint32_t row_base[kRowsPerThread];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < kRowsPerThread; ++h) {
       const int k = rr + 8 * h;
       row_base[h] = (uint32_t)(((4 * jp) >> 3) * kLbo + (k >> 3) * kSbo + (k & 7) * 128);
     }
     uint32_t chunk_off[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) chunk_off[e] = ((c0 + (uint32_t)e) ^ rsw) << 4;
+    // plane words of the thread's rows (the TMA swizzles the 128-byte plane rows: 16-byte
+    // chunk c of row r at chunk c ^ (r & 7)); the same offset in every stage
+    const uint32_t poff =
+        (uint32_t)(rr * (TW * 4)) + ((((uint32_t)jp >> 1) ^ (uint32_t)(rr & 7)) << 4) + (uint32_t)(jp & 1) * 8u;
+
+    // code bytes of one merged word -> dtype(code * s) for its 16 columns, as 8 packed
+    // pairs (columns 4t + 2p, 4t + 2p + 1): exact code in fp32, packed to the dtype
+    // (|code| <= 128 is exact there), one rounded multiply by the scale pair
+    auto convert = [&](const uint32_t (&q)[4], const uint32_t (&sc)[8], uint32_t (&o)[8]) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float2 f = make_float2(__int_as_float(__byte_perm(q[t], kMagicBits, 0x7440u | (2u * p))),
+                                       __int_as_float(__byte_perm(q[t], kMagicBits, 0x7440u | (2u * p + 1u))));
+          const float2 c = __fadd2_rn(f, make_float2(-kMagic, -kMagic));
+          o[2 * t + p] = Fmt<T>::mul2(Fmt<T>::pack(c.x, c.y), sc[2 * t + p]);
+        }
+      }
+    };
 
     for (int i = 0; i < nq; ++i) {
       const int q = q0 + i, s = i % SW, ps = i % SP;
-      if (i > 0 && q % spg == 0) {  // next scale group: its scales were prefetched
+      if (q == g_next) {  // next scale group: its scales were prefetched
         unpack_scales();
-        const int g = q / spg;
-        if ((g + 1) * spg < q0 + nq) load_scales(g + 1);
+        g_next += spg;
+        if (g_next < q0 + nq) load_scales(g_next / spg);
       }
-      if (i >= SW) mbar_wait(&empty[s], ((i / SW) - 1) & 1);
-      mbar_wait(&p_full[ps], (i / SP) & 1);
-      // plane words of the two words of rows rr, rr + 8 (the planes are 128-byte
-      // swizzled by the TMA: 16-byte chunk c of row r sits at chunk c ^ (r & 7))
-      uint2 P[2][4];
-      const unsigned char* pst =
-          sP + ps * kStageP + rr * (TW * 4) + ((((uint32_t)jp >> 1) ^ (uint32_t)(rr & 7)) << 4) + (jp & 1) * 8;
+      if (i >= SW) mbar_wait_inline(&empty[s], ((i / SW) - 1) & 1);
+      mbar_wait_inline(&p_full[ps], (i / SP) & 1);
+      uint2 P[kRowsPerThread][4];
+      const unsigned char* pst = sP + ps * kStageP + poff;
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int h = 0; h < kRowsPerThread; ++h)
 #pragma unroll
         for (int z = 0; z < 4; ++z)
           P[h][z] = z < NZ ? *reinterpret_cast<const uint2*>(pst + h * 8 * (TW * 4) + z * kPlaneBytes)
@@ -288,33 +327,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       unsigned char* wst = sW + s * kStageW;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < kRowsPerThread; ++h) {
         uint32_t qa[4], qb[4];  // merged code bytes of word 2 jp (a) and 2 jp + 1 (b)
         merge_planes(P[h][0].x ^ kSignFlip, P[h][1].x, P[h][2].x, P[h][3].x, qa);
         merge_planes(P[h][0].y ^ kSignFlip, P[h][1].y, P[h][2].y, P[h][3].y, qb);
         uint32_t oa[8], ob[8];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float2 v[4];  // column 4t + L of (word a, word b) times its scale
-#pragma unroll
-          for (int L = 0; L < 4; ++L) {
-            const uint32_t sel = 0x7440u | (uint32_t)L;
-            const float2 f = make_float2(__int_as_float(__byte_perm(qa[t], kMagicBits, sel)),
-                                         __int_as_float(__byte_perm(qb[t], kMagicBits, sel)));
-            if constexpr (Fmt<T>::v == 1) {
-              // bf16 scale (8 significant bits): (2^23 + 128) * s / 2^shift is exact in
-              // fp32, so one fused multiply-add gives code * s exactly
-              v[L] = __ffma2_rn(f, sreg[4 * t + L], sneg[4 * t + L]);
-            } else {
-              v[L] = __fmul2_rn(__fadd2_rn(f, make_float2(-kMagic, -kMagic)), sreg[4 * t + L]);
-            }
-          }
-          // code * s exactly in fp32, rounded once to the activation dtype (kernel.py:586)
-          oa[2 * t] = Fmt<T>::pack(v[0].x, v[1].x);
-          oa[2 * t + 1] = Fmt<T>::pack(v[2].x, v[3].x);
-          ob[2 * t] = Fmt<T>::pack(v[0].y, v[1].y);
-          ob[2 * t + 1] = Fmt<T>::pack(v[2].y, v[3].y);
-        }
+        convert(qa, sa, oa);  // dtype(code * s) rounded once (kernel.py:586)
+        convert(qb, sb, ob);
         unsigned char* rowp = wst + row_base[h];
         *reinterpret_cast<uint4*>(rowp + chunk_off[0]) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
         *reinterpret_cast<uint4*>(rowp + chunk_off[1]) = make_uint4(oa[4], oa[5], oa[6], oa[7]);
@@ -337,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* part = reinterpret_cast<float*>(smem);  // the stages are idle now
     const int quarter = warp & 3;
 #pragma unroll 1
-    for (int blk = warp >> 2; blk < 4; blk += 2) {
+    for (int blk = warp >> 2; blk < 4; blk += kConvWarps / 4) {
       const int pos = blk * 128 + quarter * 32 + lane;
       const int pw = pos >> 4, pc = pos & 15;
       for (int h = 0; h < (int)cstride; h += 32) {

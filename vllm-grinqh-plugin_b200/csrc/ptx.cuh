@@ -95,6 +95,13 @@ static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// mbar_wait with its first try inline: no call on the common path, where the phase
+// completes within the try's hardware suspend window.
+__device__ __forceinline__ bool mbar_wait_inline(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait(bar, parity);
+}
+
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from global
 // to this CTA's shared memory; completion is counted on `bar` (complete_tx).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
