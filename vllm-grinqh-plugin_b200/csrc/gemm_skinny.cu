@@ -22,9 +22,9 @@
 // converter warps per scheduler (96 registers a thread) hide the latency of that
 // chain. Warp 16 loads the planes; warp 17 issues the MMAs (per 16-deep K slice, one
 // tcgen05.mma kind::f16 per 128-column block, N = Mp) from one thread into TMEM;
-// tcgen05.commit frees the stage, and a second lane of warp 17 then loads the x tile
-// of the step that reuses it (the x loads stay off the plane loader's TMA queue and
-// out of the converters' loop). The converters never wait on global memory: the
+// tcgen05.commit frees the stage, and warp 18 then loads the x tile of the step that
+// reuses it (the x loads stay off the plane loader's TMA queue and out of the
+// converters' loop). The converters never wait on global memory: the
 // plane ring hides its latency.
 //
 // K is split over the CTAs of a thread-block cluster (and over several clusters for
@@ -66,8 +66,8 @@ constexpr int SP = 5, SW = 4;  // plane stages; weight / activation stages
 constexpr int kConvWarps = GRINQH_SKINNY_CONV_WARPS;  // 8 (two rows a thread) or 16 (one row)
 static_assert(kConvWarps == 8 || kConvWarps == 16, "converter warps");
 constexpr int kRowsPerThread = 16 / kConvWarps;       // rows of a step per converter thread
-constexpr int kLoadWarp = kConvWarps, kMmaWarp = kConvWarps + 1;
-constexpr int kThreads = 32 * (kConvWarps + 2);
+constexpr int kLoadWarp = kConvWarps, kMmaWarp = kConvWarps + 1, kXWarp = kConvWarps + 2;
+constexpr int kThreads = 32 * (kConvWarps + 3);
 constexpr int kMaxMp = 64;
 constexpr uint32_t kPlaneBytes = BK * TW * 4;  // one plane of a step: 4 KB
 constexpr uint32_t kStageP = 4 * kPlaneBytes;  // 16 KB
@@ -216,9 +216,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&empty[s]);
       }
       mma_commit(acc_full);
-    } else if (lane == 1) {
-      // activations: x of step i into stage i % SW as soon as the MMAs of step i - SW
-      // have released it, so the load is in flight well before the MMAs need it
+    }
+    __syncwarp();
+  } else if (warp == kXWarp) {
+    // ------------------------------------------------------------ activation loader
+    // x of step i into stage i % SW as soon as the MMAs of step i - SW have released
+    // it, so the load is in flight well before the MMAs need it. A warp of its own: a
+    // lane of the MMA warp waiting on a barrier would hold back a lane of the same warp
+    // that must act for the barrier to complete.
+    if (lane == 0) {
       prefetch_tmap(&tmap_x);
       const uint32_t xbytes = (uint32_t)mp * BK * 2;
       for (int i = 0; i < nq; ++i) {
