@@ -393,7 +393,7 @@ bool m1_supported(int64_t M, int64_t K, int64_t N, int group) {
   return M == 1 && N % 32 == 0 && K % group == 0 && group % kD == 0;
 }
 
-static M1Plan plan_for(int64_t K, int64_t N, int64_t target) {
+static M1Plan plan_for(int64_t K, int64_t N, int64_t target, bool few_slots) {
   M1Plan p{};
   const int64_t n16 = N / 16;
   p.tiles = (int)((n16 + kSliceW - 1) / kSliceW);
@@ -401,7 +401,20 @@ static M1Plan plan_for(int64_t K, int64_t N, int64_t target) {
   const int64_t max_splits = (K + kWarps * kD - 1) / (kWarps * kD);
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
-  p.cluster = (int)(splits < 8 ? splits : 8);
+  // Cluster size: the split count is rounded down to a multiple of it, and larger
+  // clusters leave fewer fp32 slots for the last CTA to add. Measured on the Llama
+  // shapes (µs, clusters of 8 / 4 / 2): qkv 16.2 / 14.5 / 16.2, o 14.9 / 12.7 / 14.4,
+  // gate_up 35.6 / 38.4 / 33.2, down 23.2 / 22.3 / 24.4. So clusters of 4 where they
+  // keep more splits than clusters of 8, else clusters of 2 where those do, else 8.
+  if (splits < 8 || few_slots) {
+    p.cluster = (int)(splits < 8 ? splits : 8);
+  } else if (splits / 4 * 4 > splits / 8 * 8) {
+    p.cluster = 4;
+  } else if (splits / 2 * 2 > splits / 8 * 8) {
+    p.cluster = 2;
+  } else {
+    p.cluster = 8;
+  }
   splits = splits / p.cluster * p.cluster;
   int64_t rpw = ((K + splits - 1) / splits + kWarps - 1) / kWarps;
   rpw = (rpw + kD - 1) / kD * kD;
@@ -457,7 +470,7 @@ static int resident_clusters(int cluster, size_t smem) {
   return n;
 }
 
-M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
+M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count, bool few_slots) {
   // One wave: 2 CTAs fit per SM, and a target of 1.9 CTAs per SM measured best on a
   // 148-SM B200. Clusters live inside one GPC, so 8-CTA clusters do not tile all SMs:
   // a grid with more clusters than the device holds at once would run the rest as a
@@ -466,13 +479,13 @@ M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count) {
   // device to ask (host-only queries) the first plan stands.
   (void)group;
   int64_t target = (int64_t)(sm_count > 0 ? sm_count : 148) * 19 / 10;
-  M1Plan p = plan_for(K, N, target);
+  M1Plan p = plan_for(K, N, target, few_slots);
   for (;;) {
     const int have = resident_clusters(p.cluster, p.smem_bytes);
     if (have <= 0 || (int64_t)p.tiles * p.grid_splits <= (int64_t)have * p.cluster) return p;
     if (p.grid_splits <= p.cluster) return p;  // one cluster per tile is the least
     target = (int64_t)p.tiles * (p.grid_splits - p.cluster);
-    const M1Plan q = plan_for(K, N, target);
+    const M1Plan q = plan_for(K, N, target, few_slots);
     if ((int64_t)q.tiles * q.grid_splits >= (int64_t)p.tiles * p.grid_splits) return p;
     p = q;
   }

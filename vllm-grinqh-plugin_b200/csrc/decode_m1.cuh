@@ -37,7 +37,9 @@ bool m1_supported(int64_t M, int64_t K, int64_t N, int group);
 inline bool m1_pointers_ok(const void* w, const void* s) {
   return (reinterpret_cast<uintptr_t>(w) % 8) == 0 && (reinterpret_cast<uintptr_t>(s) % 4) == 0;
 }
-M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count);
+// few_slots: clusters of 8 CTAs wherever the split count allows, for the fewest fp32
+// slots (the fixed scratch of grinqh_gemv_noalloc), at some cost in time.
+M1Plan plan_m1(int64_t K, int64_t N, int group, int sm_count, bool few_slots = false);
 // the plan's shared memory fits one CTA (rows_per_cta grows with K when N is so wide
 // that the column slices alone fill the GPU)
 inline bool m1_plan_fits(const M1Plan& p) { return p.smem_bytes <= 227u * 1024u; }

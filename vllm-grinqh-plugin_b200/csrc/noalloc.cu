@@ -77,7 +77,7 @@ extern "C" int grinqh_gemv_noalloc(const void* x, int dtype, int64_t K, const ui
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
-  const M1Plan plan = plan_m1(K, N, group, sms);
+  const M1Plan plan = plan_m1(K, N, group, sms, /*few_slots=*/true);
   if (!m1_plan_fits(plan))
     return set_error(GRINQH_ERR_UNSUPPORTED, "K=%lld N=%lld: the GEMV's shared memory does not fit one CTA (use "
                      "grinqh_gemm_or_gemv)", (long long)K, (long long)N);
